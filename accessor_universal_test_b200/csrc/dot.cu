@@ -1,0 +1,518 @@
+// dot.cu -- the decode-fused DOT kernels and aut_dot / aut_dot_batched.
+//
+// One persistent kernel per (format, layout, accumulator) does the whole
+// DOT: 128-bit vector loads of both code streams, in-register decode, FMA
+// into per-thread accumulators, a warp-shuffle + shared-memory block sum and
+// a single-pass grid reduction into the device result.  This replaces the
+// reference's dot_thread_kernel + finalize_dot_kernel pair
+// (bitwidth_benchmark_kernels.cuh:403-457), the LNS dot_thread_kernel
+// (lns_benchmark_kernels.cuh:80-131), raw_dot_kernel (:681-703) and the
+// accessor map-reduce (src/accessor_dot_bench.cu:417-454).
+#include "dot_device.cuh"
+#include "internal.hpp"
+
+#include <cuda_fp16.h>
+
+#include <cstdio>
+#include <cstring>
+
+namespace aut::dev {
+
+struct dot_params {
+  const unsigned char *x;
+  const unsigned char *y;
+  uint64_t n;
+  uint64_t batch_stride;  // bytes between the pairs of a batch
+  int vector_ok;          // both streams 16-byte aligned
+  const void *table;      // decode table (LNS formats)
+  double *partials;       // [gridDim.y][gridDim.x]
+  unsigned int *tickets;  // [gridDim.y]
+  double *results;        // [gridDim.y]
+};
+
+// ---------------------------------------------------------------------------
+// Codecs.  Each supplies: kS (bits per stored slot), kU (packets per thread
+// per tile), kTableBytes (dynamic shared memory), prepare(), packet() for a
+// whole packet in registers and scalar() for ragged tails.
+// ---------------------------------------------------------------------------
+
+// IEEE-like formats with an 8-bit exponent (e8m0 ... e8m15, bf16, and raw
+// FP32 as W = 32): the FP32 bit pattern is the code shifted to the top of
+// the word (decoder_strategy_core.hpp:319-322), exact for normals,
+// subnormals, infinities and NaNs.
+template <int S, int W> struct e8_codec {
+  static constexpr int kS = S;
+  static constexpr int kU = packet_shape<S>::Q == 1 ? 4 : (S == 24 ? 2 : 1);
+  static constexpr int kTableBytes = 0;
+  __device__ static void prepare(const void *, unsigned char *) {}
+
+  template <class Acc>
+  __device__ __forceinline__ static void packet(const uint32_t *xw,
+                                                const uint32_t *yw, Acc &acc,
+                                                const unsigned char *) {
+    constexpr int P = packet_shape<S>::P;
+#pragma unroll
+    for (int v = 0; v < P; ++v) {
+      const float a = __uint_as_float(field_top<S, W>(xw, v));
+      const float b = __uint_as_float(field_top<S, W>(yw, v));
+      acc.mac(v, a, b);
+    }
+  }
+
+  template <class Acc>
+  __device__ __forceinline__ static void scalar(const unsigned char *xb,
+                                                const unsigned char *yb,
+                                                uint64_t i, Acc &acc,
+                                                const unsigned char *) {
+    const float a = __uint_as_float(load_code<S, W>(xb, i) << (32 - W));
+    const float b = __uint_as_float(load_code<S, W>(yb, i) << (32 - W));
+    acc.mac_d(0, static_cast<double>(a), static_cast<double>(b));
+  }
+};
+
+// Raw binary64 storage.
+struct f64_codec {
+  static constexpr int kS = 64;
+  static constexpr int kU = 4;
+  static constexpr int kTableBytes = 0;
+  __device__ static void prepare(const void *, unsigned char *) {}
+
+  template <class Acc>
+  __device__ __forceinline__ static void packet(const uint32_t *xw,
+                                                const uint32_t *yw, Acc &acc,
+                                                const unsigned char *) {
+#pragma unroll
+    for (int v = 0; v < 2; ++v) {
+      const double a = __hiloint2double(static_cast<int>(xw[2 * v + 1]),
+                                        static_cast<int>(xw[2 * v]));
+      const double b = __hiloint2double(static_cast<int>(yw[2 * v + 1]),
+                                        static_cast<int>(yw[2 * v]));
+      acc.mac_d(v, a, b);
+    }
+  }
+
+  template <class Acc>
+  __device__ __forceinline__ static void scalar(const unsigned char *xb,
+                                                const unsigned char *yb,
+                                                uint64_t i, Acc &acc,
+                                                const unsigned char *) {
+    acc.mac_d(0, __ldg(reinterpret_cast<const double *>(xb) + i),
+              __ldg(reinterpret_cast<const double *>(yb) + i));
+  }
+};
+
+// FP6 E2M3 (finite).  Four 6-bit codes are spread into the low 6 bits of four
+// bytes, the hardware converts byte pairs to f16x2 exactly, and the
+// mixed-precision FMA multiplies two f16 values exactly into an FP32
+// accumulator.  Every e2m3 value is k/8 with |k| <= 60, so products are
+// multiples of 2^-6 below 57 and an FP32 sum of up to 64 of them is exact:
+// the accumulators are carried into FP64 once per packet, which makes the
+// DOT exact up to its final rounding for both accumulator kinds.
+template <int S> struct e2m3_codec {
+  static_assert(S == 6 || S == 8, "dense 6-bit or one code per byte");
+  static constexpr int kS = S;
+  static constexpr int kU = S == 8 ? 4 : 1;
+  static constexpr int kTableBytes = 0;
+  __device__ static void prepare(const void *, unsigned char *) {}
+
+  // Codes 4g .. 4g+3 of the packet, one per byte (low 6 bits).
+  __device__ __forceinline__ static uint32_t bytes4(const uint32_t *w, int g) {
+    if constexpr (S == 8) {
+      return w[g] & 0x3f3f3f3fu;
+    } else {
+      const uint32_t q = field_low<24, 24>(w, g);    // v3 v2 v1 v0, 6 bits each
+      const uint32_t p = q + (q & 0x00fff000u) * 15u; // v1v0 -> [0,12), v3v2 -> [16,28)
+      return p + (p & 0x0fc00fc0u) * 3u;             // each code at a byte
+    }
+  }
+
+  __device__ __forceinline__ static uint32_t to_f16x2(uint32_t two_bytes) {
+    uint32_t h2;
+    asm("cvt.rn.f16x2.e2m3x2 %0, %1;"
+        : "=r"(h2)
+        : "h"(static_cast<unsigned short>(two_bytes)));
+    return h2;
+  }
+
+  __device__ __forceinline__ static void fma2(float &lo, float &hi, uint32_t x2,
+                                              uint32_t y2) {
+    asm("{\n\t.reg .f16 xl, xh, yl, yh;\n\t"
+        "mov.b32 {xl, xh}, %2;\n\t"
+        "mov.b32 {yl, yh}, %3;\n\t"
+        "fma.rn.f32.f16 %0, xl, yl, %0;\n\t"
+        "fma.rn.f32.f16 %1, xh, yh, %1;\n\t}"
+        : "+f"(lo), "+f"(hi)
+        : "r"(x2), "r"(y2));
+  }
+
+  template <class Acc>
+  __device__ __forceinline__ static void packet(const uint32_t *xw,
+                                                const uint32_t *yw, Acc &acc,
+                                                const unsigned char *) {
+    constexpr int G = packet_shape<S>::P / 4;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const uint32_t bx = bytes4(xw, g);
+      const uint32_t by = bytes4(yw, g);
+      fma2(s0, s1, to_f16x2(bx), to_f16x2(by));
+      fma2(s2, s3, to_f16x2(bx >> 16), to_f16x2(by >> 16));
+    }
+    acc.add_exact((static_cast<double>(s0) + static_cast<double>(s1)) +
+                  (static_cast<double>(s2) + static_cast<double>(s3)));
+  }
+
+  __device__ __forceinline__ static float decode1(uint32_t c) {
+    const uint32_t h2 = to_f16x2(c & 0x3fu);
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(h2)));
+  }
+
+  template <class Acc>
+  __device__ __forceinline__ static void scalar(const unsigned char *xb,
+                                                const unsigned char *yb,
+                                                uint64_t i, Acc &acc,
+                                                const unsigned char *) {
+    acc.mac_d(0, static_cast<double>(decode1(load_code<S, 6>(xb, i))),
+              static_cast<double>(decode1(load_code<S, 6>(yb, i))));
+  }
+};
+
+// lns8_r3 (one code per byte): a full 256-entry decode table, replicated
+// once per lane in shared memory (entry e of lane l at word e*32 + l), so
+// that a warp's 32 lookups hit 32 different banks.  Table values come from
+// the host exp2f / exp2 and are the reference's decoded values bit for bit.
+template <typename T> struct lns8_codec {
+  static constexpr int kS = 8;
+  static constexpr int kU = 4;
+  static constexpr int kTableBytes = 256 * 32 * static_cast<int>(sizeof(T));
+  __device__ static void prepare(const void *table, unsigned char *smem) {
+    const T *g = static_cast<const T *>(table);
+    T *s = reinterpret_cast<T *>(smem);
+    for (int e = threadIdx.x; e < 256 * 32; e += kThreads) s[e] = g[e >> 5];
+  }
+
+  template <class Acc>
+  __device__ __forceinline__ static void packet(const uint32_t *xw,
+                                                const uint32_t *yw, Acc &acc,
+                                                const unsigned char *smem) {
+    const T *tab = reinterpret_cast<const T *>(smem) + (threadIdx.x & 31);
+#pragma unroll
+    for (int v = 0; v < 16; ++v) {
+      const T a = tab[field_low<8, 8>(xw, v) << 5];
+      const T b = tab[field_low<8, 8>(yw, v) << 5];
+      if constexpr (sizeof(T) == 4)
+        acc.mac(v, a, b);
+      else
+        acc.mac_d(v, a, b);
+    }
+  }
+
+  template <class Acc>
+  __device__ __forceinline__ static void scalar(const unsigned char *xb,
+                                                const unsigned char *yb,
+                                                uint64_t i, Acc &acc,
+                                                const unsigned char *smem) {
+    const T *tab = reinterpret_cast<const T *>(smem) + (threadIdx.x & 31);
+    acc.mac_d(0, static_cast<double>(tab[load_code<8, 8>(xb, i) << 5]),
+              static_cast<double>(tab[load_code<8, 8>(yb, i) << 5]));
+  }
+};
+
+// lns16_r11: value = +-2^q * T[f] with log code c = 2048 q + f, T[f] =
+// exp2f(f / 2048) (or exp2 for FP64) from a 2048-entry shared table; the
+// power of two is an exponent-field add, exact because T[f] is in [1, 2) and
+// |q| <= 8.  The reserved code (+: zero, -: NaN) is selected explicitly.
+template <typename T> struct lns16_codec {
+  static constexpr int kS = 16;
+  static constexpr int kU = 4;
+  static constexpr int kTableBytes = 2048 * static_cast<int>(sizeof(T));
+  __device__ static void prepare(const void *table, unsigned char *smem) {
+    const T *g = static_cast<const T *>(table);
+    T *s = reinterpret_cast<T *>(smem);
+    for (int e = threadIdx.x; e < 2048; e += kThreads) s[e] = g[e];
+  }
+
+  __device__ __forceinline__ static T decode(uint32_t c, const T *tab) {
+    const int q = static_cast<int>(c << 17) >> 28;
+    const uint32_t sign = c & 0x8000u;
+    const bool special = (c & 0x7fffu) == 0x4000u;
+    if constexpr (sizeof(T) == 4) {
+      const uint32_t bits =
+          (__float_as_uint(tab[c & 0x7ffu]) + (static_cast<uint32_t>(q) << 23)) |
+          (sign << 16);
+      const uint32_t out = special ? (sign ? 0x7fc00000u : 0u) : bits;
+      return __uint_as_float(out);
+    } else {
+      const double t = tab[c & 0x7ffu];
+      const uint32_t hi =
+          (static_cast<uint32_t>(__double2hiint(t)) + (static_cast<uint32_t>(q) << 20)) |
+          (sign << 16);
+      const uint32_t lo = static_cast<uint32_t>(__double2loint(t));
+      const uint32_t ho = special ? (sign ? 0x7ff80000u : 0u) : hi;
+      const uint32_t lo2 = special ? 0u : lo;
+      return __hiloint2double(static_cast<int>(ho), static_cast<int>(lo2));
+    }
+  }
+
+  template <class Acc>
+  __device__ __forceinline__ static void packet(const uint32_t *xw,
+                                                const uint32_t *yw, Acc &acc,
+                                                const unsigned char *smem) {
+    const T *tab = reinterpret_cast<const T *>(smem);
+#pragma unroll
+    for (int v = 0; v < 8; ++v) {
+      const T a = decode(field_low<16, 16>(xw, v), tab);
+      const T b = decode(field_low<16, 16>(yw, v), tab);
+      if constexpr (sizeof(T) == 4)
+        acc.mac(v, a, b);
+      else
+        acc.mac_d(v, a, b);
+    }
+  }
+
+  template <class Acc>
+  __device__ __forceinline__ static void scalar(const unsigned char *xb,
+                                                const unsigned char *yb,
+                                                uint64_t i, Acc &acc,
+                                                const unsigned char *smem) {
+    const T *tab = reinterpret_cast<const T *>(smem);
+    acc.mac_d(0, static_cast<double>(decode(load_code<16, 16>(xb, i), tab)),
+              static_cast<double>(decode(load_code<16, 16>(yb, i), tab)));
+  }
+};
+
+// ---------------------------------------------------------------------------
+// The kernel.
+// ---------------------------------------------------------------------------
+template <class Codec, class Acc>
+__global__ void __launch_bounds__(kThreads)
+    dot_kernel(const dot_params p) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ double scratch[kThreads / 32];
+  constexpr int S = Codec::kS;
+  constexpr int Q = packet_shape<S>::Q;
+  constexpr int P = packet_shape<S>::P;
+  constexpr int U = Codec::kU;
+  constexpr uint64_t tile_packets = static_cast<uint64_t>(kThreads) * U;
+
+  const unsigned int batch = blockIdx.y;
+  const unsigned char *xb = p.x + batch * p.batch_stride;
+  const unsigned char *yb = p.y + batch * p.batch_stride;
+
+  if constexpr (Codec::kTableBytes > 0) {
+    Codec::prepare(p.table, smem);
+    __syncthreads();
+  }
+
+  Acc acc;
+  const uint64_t tiles = p.vector_ok ? (p.n / P) / tile_packets : 0;
+  const uint4 *X = reinterpret_cast<const uint4 *>(xb);
+  const uint4 *Y = reinterpret_cast<const uint4 *>(yb);
+  for (uint64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const uint64_t first = t * tile_packets + threadIdx.x;
+    uint4 xv[U][Q], yv[U][Q];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+#pragma unroll
+      for (int q = 0; q < Q; ++q) {
+        xv[u][q] = __ldg(X + (first + static_cast<uint64_t>(u) * kThreads) * Q + q);
+        yv[u][q] = __ldg(Y + (first + static_cast<uint64_t>(u) * kThreads) * Q + q);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      Codec::packet(reinterpret_cast<const uint32_t *>(xv[u]),
+                    reinterpret_cast<const uint32_t *>(yv[u]), acc, smem);
+    acc.flush();
+  }
+
+  // Ragged tail (everything when a pointer is not 16-byte aligned).
+  const uint64_t done = tiles * tile_packets * P;
+  for (uint64_t i = done + static_cast<uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
+       i < p.n; i += static_cast<uint64_t>(gridDim.x) * kThreads)
+    Codec::scalar(xb, yb, i, acc, smem);
+
+  const double s = block_sum(acc.value(), scratch);
+  grid_finish(s, p.partials + static_cast<uint64_t>(batch) * gridDim.x,
+              p.tickets + batch, p.results + batch, scratch);
+}
+
+} // namespace aut::dev
+
+// ---------------------------------------------------------------------------
+// Host-side dispatch.
+// ---------------------------------------------------------------------------
+namespace aut::lib {
+namespace {
+
+using kernel_fn = void (*)(aut::dev::dot_params);
+
+struct kernel_entry {
+  kernel_fn fn = nullptr;
+  int smem = 0;
+  int stride = 0;      // bits per stored slot
+  int table_kind = 0;  // 0 none, 1 lns full f32, 2 lns full f64, 3 frac f32, 4 frac f64
+  int packets_per_thread = 1;
+  int blocks_per_sm = 0;
+};
+
+template <class Codec, class Acc> kernel_entry make_entry(int table_kind) {
+  kernel_entry e;
+  e.fn = aut::dev::dot_kernel<Codec, Acc>;
+  e.smem = Codec::kTableBytes;
+  e.stride = Codec::kS;
+  e.table_kind = table_kind;
+  e.packets_per_thread = Codec::kU;
+  return e;
+}
+
+template <class Codec> kernel_entry pick(int accum, int table_kind) {
+  return accum == AUT_ACCUM_FP32 ? make_entry<Codec, aut::dev::acc_f32>(table_kind)
+                                 : make_entry<Codec, aut::dev::acc_f64>(table_kind);
+}
+
+kernel_entry lookup(int32_t format, int32_t layout, int32_t accum) {
+  using namespace aut::dev;
+  const bool dense = layout == AUT_LAYOUT_DENSE;
+  switch (format) {
+  case AUT_FMT_FP32: return pick<e8_codec<32, 32>>(accum, 0);
+  case AUT_FMT_FP64:
+    if (accum != AUT_ACCUM_FP64) return {};
+    return make_entry<f64_codec, acc_f64>(0);
+  case AUT_FMT_E2M3:
+    return dense ? pick<e2m3_codec<6>>(accum, 0) : pick<e2m3_codec<8>>(accum, 0);
+  case AUT_FMT_E8M0:
+    return dense ? pick<e8_codec<9, 9>>(accum, 0) : pick<e8_codec<16, 9>>(accum, 0);
+  case AUT_FMT_E8M1:
+    return dense ? pick<e8_codec<10, 10>>(accum, 0) : pick<e8_codec<16, 10>>(accum, 0);
+  case AUT_FMT_E8M3:
+    return dense ? pick<e8_codec<12, 12>>(accum, 0) : pick<e8_codec<16, 12>>(accum, 0);
+  case AUT_FMT_E8M5:
+    return dense ? pick<e8_codec<14, 14>>(accum, 0) : pick<e8_codec<16, 14>>(accum, 0);
+  case AUT_FMT_BF16_E8M7: return pick<e8_codec<16, 16>>(accum, 0);
+  case AUT_FMT_E8M15:
+    return dense ? pick<e8_codec<24, 24>>(accum, 0) : pick<e8_codec<32, 24>>(accum, 0);
+  case AUT_FMT_LNS8_R3:
+    return accum == AUT_ACCUM_FP32 ? make_entry<lns8_codec<float>, acc_f32>(1)
+                                   : make_entry<lns8_codec<double>, acc_f64>(2);
+  case AUT_FMT_LNS16_R11:
+    return accum == AUT_ACCUM_FP32 ? make_entry<lns16_codec<float>, acc_f32>(3)
+                                   : make_entry<lns16_codec<double>, acc_f64>(4);
+  default: return {};
+  }
+}
+
+// Occupancy of each kernel, cached per function pointer.
+struct occupancy_cache {
+  std::mutex mutex;
+  kernel_fn fns[128] = {};
+  int blocks[128] = {};
+  int count = 0;
+};
+occupancy_cache &cache() {
+  static occupancy_cache c;
+  return c;
+}
+
+aut_status blocks_per_sm(kernel_entry &e) {
+  auto &c = cache();
+  std::lock_guard<std::mutex> lock(c.mutex);
+  for (int k = 0; k < c.count; ++k)
+    if (c.fns[k] == e.fn) {
+      e.blocks_per_sm = c.blocks[k];
+      return AUT_OK;
+    }
+  if (e.smem > 48 * 1024)
+    AUT_CUDA_TRY(cudaFuncSetAttribute(reinterpret_cast<const void *>(e.fn),
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      e.smem));
+  int b = 0;
+  AUT_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+      &b, reinterpret_cast<const void *>(e.fn), aut::dev::kThreads, e.smem));
+  if (b < 1) return fail(AUT_ERR_UNSUPPORTED, "kernel does not fit on an SM");
+  if (c.count < 128) {
+    c.fns[c.count] = e.fn;
+    c.blocks[c.count] = b;
+    ++c.count;
+  }
+  e.blocks_per_sm = b;
+  return AUT_OK;
+}
+
+uint64_t packet_values(int stride) {
+  int g = stride, b = 128;
+  while (b != 0) {
+    const int r = g % b;
+    g = b;
+    b = r;
+  }
+  return static_cast<uint64_t>(128 / g);
+}
+
+} // namespace
+
+int32_t dot_supported(int32_t format, int32_t layout, int32_t accum) {
+  if (layout != AUT_LAYOUT_DENSE && layout != AUT_LAYOUT_PADDED) return 0;
+  if (accum != AUT_ACCUM_FP32 && accum != AUT_ACCUM_FP64) return 0;
+  return lookup(format, layout, accum).fn != nullptr ? 1 : 0;
+}
+
+aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
+                      int32_t accum, const void *x, const void *y, uint64_t n,
+                      uint32_t batch, uint64_t batch_stride, double *results,
+                      void *stream, double *partials, unsigned int *tickets,
+                      int max_blocks_total) {
+  kernel_entry e = lookup(format, layout, accum);
+  if (e.fn == nullptr)
+    return fail(AUT_ERR_UNSUPPORTED,
+                "no fused DOT kernel for this format/layout/accumulator");
+  aut_status st = blocks_per_sm(e);
+  if (st != AUT_OK) return st;
+
+  const void *table = nullptr;
+  if (e.table_kind != 0) {
+    const lns_tables *t = nullptr;
+    st = lns_tables_for(ws, format, &t);
+    if (st != AUT_OK) return st;
+    table = e.table_kind == 1   ? static_cast<const void *>(t->full_f32)
+            : e.table_kind == 2 ? static_cast<const void *>(t->full_f64)
+            : e.table_kind == 3 ? static_cast<const void *>(t->frac_f32)
+                                : static_cast<const void *>(t->frac_f64);
+  }
+
+  const uint64_t P = packet_values(e.stride);
+  const uint64_t tile_values =
+      P * aut::dev::kThreads * static_cast<uint64_t>(e.packets_per_thread);
+  const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(y) % 16 == 0) &&
+                       (batch <= 1 || batch_stride % 16 == 0);
+  const int cap = ws->sm_count * e.blocks_per_sm;
+  uint64_t wanted = aligned ? (n / tile_values) : 0;
+  if (wanted == 0) wanted = (n + aut::dev::kThreads - 1) / aut::dev::kThreads;
+  if (wanted == 0) wanted = 1;
+  for (uint32_t b0 = 0; b0 < batch; b0 += kMaxBatchPerLaunch) {
+    const uint32_t nb = batch - b0 < static_cast<uint32_t>(kMaxBatchPerLaunch)
+                            ? batch - b0
+                            : static_cast<uint32_t>(kMaxBatchPerLaunch);
+    int per_pair = static_cast<int>((cap + nb - 1) / nb);
+    if (per_pair < 1) per_pair = 1;
+    if (static_cast<uint64_t>(per_pair) > wanted) per_pair = static_cast<int>(wanted);
+    if (per_pair > max_blocks_total) per_pair = max_blocks_total;
+    aut::dev::dot_params p;
+    p.x = static_cast<const unsigned char *>(x) + static_cast<uint64_t>(b0) * batch_stride;
+    p.y = static_cast<const unsigned char *>(y) + static_cast<uint64_t>(b0) * batch_stride;
+    p.n = n;
+    p.batch_stride = batch_stride;
+    p.vector_ok = aligned ? 1 : 0;
+    p.table = table;
+    p.partials = partials;
+    p.tickets = tickets;
+    p.results = results + b0;
+    dim3 grid(static_cast<unsigned>(per_pair), nb);
+    e.fn<<<grid, aut::dev::kThreads, e.smem, static_cast<cudaStream_t>(stream)>>>(p);
+    AUT_CUDA_TRY(cudaGetLastError());
+  }
+  return AUT_OK;
+}
+
+} // namespace aut::lib

@@ -1,0 +1,74 @@
+// internal.hpp -- declarations shared by the library's translation units.
+#ifndef AUT_INTERNAL_HPP_
+#define AUT_INTERNAL_HPP_
+
+#include "autdot.h"
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <mutex>
+#include <string>
+
+namespace aut::lib {
+
+// ---- registry ---------------------------------------------------------------
+struct format_desc {
+  const char *name;
+  int family;
+  int total_bits;
+  int exponent_bits; // LNS: log fraction bits R
+  int finite;
+};
+
+const format_desc *find_format(int32_t id); // nullptr when out of range
+int stride_bits(const format_desc &f, int layout); // bits per stored value
+int container_bits(const format_desc &f);          // padded container width
+
+// ---- errors -----------------------------------------------------------------
+aut_status fail(aut_status code, const std::string &message);
+aut_status cuda_fail(cudaError_t err, const char *what);
+void clear_error();
+
+#define AUT_CUDA_TRY(expr)                                                     \
+  do {                                                                         \
+    cudaError_t aut_err_ = (expr);                                             \
+    if (aut_err_ != cudaSuccess) return ::aut::lib::cuda_fail(aut_err_, #expr); \
+  } while (0)
+
+// ---- decode tables kept per workspace ----------------------------------------
+// LNS formats decode through host-built tables (host exp2f / exp2), so that
+// device values are bit-identical to the reference's host decoder.
+struct lns_tables {
+  int ready = 0;
+  float *full_f32 = nullptr;   // 2^B entries (B <= 16)
+  double *full_f64 = nullptr;  // 2^B entries
+  float *frac_f32 = nullptr;   // 2^R entries: exp2f(f / 2^R)
+  double *frac_f64 = nullptr;  // 2^R entries: exp2(f / 2^R)
+  double *thresholds = nullptr; // encode thresholds, 2^(B-1) - 2 entries
+  double zero_threshold = 0.0; // smallest magnitude that does not encode to 0
+};
+
+constexpr int kMaxBatchPerLaunch = 1024;
+constexpr int kLnsFormatsCached = 8;
+
+} // namespace aut::lib
+
+struct aut_workspace {
+  int device = 0;
+  int sm_count = 0;
+  int max_blocks = 0;       // per launch, all batches together
+  double *partials = nullptr; // [kMaxBatchPerLaunch * max_blocks]
+  unsigned int *tickets = nullptr; // [kMaxBatchPerLaunch], kept at zero
+  std::mutex mutex;
+  int lns_ids[aut::lib::kLnsFormatsCached] = {-1, -1, -1, -1, -1, -1, -1, -1};
+  aut::lib::lns_tables lns[aut::lib::kLnsFormatsCached];
+};
+
+namespace aut::lib {
+// Returns the tables of an LNS format, building them on first use.
+aut_status lns_tables_for(aut_workspace *ws, int32_t format_id,
+                          const lns_tables **out);
+} // namespace aut::lib
+
+#endif

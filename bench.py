@@ -1,0 +1,449 @@
+#!/usr/bin/env python3
+"""Benchmark of the decode-fused DOT library (libautdot, sm_100a).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload e8-sweep|e2m3|lns|raw] [--accum fp32|fp64]
+
+Default workload (the one the headline metric is quoted on): the E8
+truncated-float bit-width sweep -- e8m0 (9 bits; the 8-bit width has no room
+for 8 exponent bits), e8m1 (10), e8m3 (12), e8m5 (14), bf16_e8m7 (16) and
+e8m15 (24) -- stored as dense LSB-first 32-bit-word bitstreams with fields
+crossing word boundaries, N = 2^27 values per GPU, x, y uniform[-1, 1)
+(seeded, counter based), contiguous shards over GPUs, one FP64 all-reduce.
+A step is one fused DOT per format (six launches) plus, on more than one GPU,
+one NCCL all-reduce of the six FP64 partials.
+
+value    packed HBM GB/s of the whole job (2 N bits / 8 per DOT, all GPUs),
+         inputs resident in HBM; each pair is larger than the 126 MB L2 and
+         consecutive DOTs read different buffers, so no L2 flush is needed.
+e2e      the same metric through the C ABI from pinned HOST buffers: every
+         step copies the packed vectors host->device, runs the DOTs and reads
+         the FP64 results back.
+roofline the dominant kernel's packed bytes per launch / its CUDA-event
+         launch time, against the measured HBM copy bandwidth.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+N_DEFAULT = 1 << 27
+SEED = 0x243F6A8885A308D3
+HBM_FALLBACK_GBS = 6650.0
+
+WORKLOADS = {
+    # name: (description, [(format, generator kind)], layout, n per GPU)
+    "e8-sweep": ("E8 truncated-float bit-width sweep e8m0/e8m1/e8m3/e8m5/bf16_e8m7/e8m15 "
+                 "(9/10/12/14/16/24 bits), dense LSB-first u32 bitstream, x,y uniform[-1,1)",
+                 [("e8m0", 0), ("e8m1", 0), ("e8m3", 0), ("e8m5", 0), ("bf16_e8m7", 0),
+                  ("e8m15", 0)], 0, N_DEFAULT),
+    "e2m3": ("FP6 E2M3 dense (4 values per 24 bits), x,y ~ N(0,1) (Irwin-Hall), RNE encoded",
+             [("e2m3", 2)], 0, N_DEFAULT),
+    "lns": ("LNS lns8_r3 and lns16_r11, N=2^28, cancellation pair y_i = s_i x_i (1+1e-6 u_i)",
+            [("lns8_r3", 3), ("lns16_r11", 3)], 0, 1 << 28),
+    "raw": ("raw FP32 and FP64 storage DOT, x,y uniform[-1,1)",
+            [("fp32", 1), ("fp64", 0)], 0, N_DEFAULT),
+}
+METRIC = "decoded elems/s & HBM GB/s (% of 8 TB/s) at N=2^27/GPU, 1-8 GPUs; normalized err"
+
+
+def parse():
+    p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=400)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", choices=sorted(WORKLOADS), default="e8-sweep")
+    p.add_argument("--accum", choices=["fp32", "fp64"], default="fp32")
+    p.add_argument("--n", type=int, default=0, help="values per GPU (default: workload's)")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--e2e-steps", type=int, default=6)
+    return p.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def measured_peak():
+    path = os.path.join(HERE, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return HBM_FALLBACK_GBS, "fallback"
+
+
+def committed_traffic():
+    path = os.path.join(HERE, "profiles", "dram_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+# ---- clocks during the timed region ---------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def physical_gpu(local: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",")]
+        if local < len(ids) and ids[local].isdigit():
+            return int(ids[local])
+    return local
+
+
+# ---- CPU baseline (the reference's CPU path on the host cores) -------------------
+def cpu_reference_dot(fmt_name, stride, xw, yw, n, threads):
+    """The reference's host decode + compensated long-double DOT; oracle/_ref
+    when the reference was compiled here, else the oracle's restatement."""
+    sys.path.insert(0, os.path.join(HERE, "oracle"))
+    import pyoracle
+    ref = None
+    if os.path.exists(pyoracle.REF_SO):
+        ref = pyoracle.Reference()
+    if ref is not None and fmt_name in ref.formats:
+        d, s = ref.dot_dense(fmt_name, stride, xw, yw, n, threads)
+        return d, s, "reference"
+    if ref is not None and fmt_name in ("fp32", "fp64"):
+        import numpy as np
+        dt = np.float32 if fmt_name == "fp32" else np.float64
+        d, s = ref.dot_raw(xw.view(dt)[:n], yw.view(dt)[:n], threads)
+        return d, s, "reference"
+    orc = pyoracle.oracle()
+    from accessor_universal_test_b200 import _lib
+    desc = _lib.format_info(_lib.format_id(fmt_name))
+    d, s = orc.dot_dense(desc, stride, xw, yw, n, threads)
+    return d, s, "port"
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ---- the reference arm ---------------------------------------------------------
+def run_reference_arm(args, rank, world):
+    if rank != 0:
+        return 0
+    import numpy as np
+    desc, fmts, layout, n_full = WORKLOADS[args.workload]
+    from accessor_universal_test_b200 import _lib
+    threads = host_threads()
+    # Encoded inputs come from the product's host codec (no GPU needed here).
+    rng_n = 1 << 22
+    streams = []
+    sys.path.insert(0, os.path.join(HERE, "oracle"))
+    import pyoracle
+    orc = pyoracle.oracle()
+    for name, kind in fmts:
+        fid = _lib.format_id(name)
+        fam, bits, _, _ = _lib.format_info(fid)
+        x = orc.synthetic(kind, SEED, 0, rng_n)
+        y = orc.synthetic(kind, SEED, 1, rng_n)
+        if fam == _lib.FAMILY_RAW_FP64:
+            streams.append((name, 64, x.view(np.uint32), y.view(np.uint32), bits))
+            continue
+        out = []
+        for v in (x, y):
+            codes = np.empty(rng_n, np.uint32)
+            _lib.check(_lib.load().aut_encode_host(fid, v.ctypes.data, rng_n, codes.ctypes.data))
+            packed = np.zeros(_lib.storage_bytes(fid, layout, rng_n), np.uint8)
+            _lib.check(_lib.load().aut_pack_host(fid, layout, codes.ctypes.data, rng_n,
+                                                 packed.ctypes.data))
+            out.append(packed.view(np.uint32))
+        streams.append((name, bits, out[0], out[1], bits))
+
+    def one_step(m):
+        kind_used = None
+        for name, stride, xw, yw, _ in streams:
+            _, _, kind_used = cpu_reference_dot(name, stride, xw, yw, m, threads)
+        return kind_used
+
+    # size the per-step sample so that the whole run stays within ~2 minutes
+    t0 = time.perf_counter()
+    one_step(1 << 16)
+    per_value = (time.perf_counter() - t0) / (1 << 16)
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    m = int(min(rng_n, max(1 << 12, budget / max(per_value, 1e-12))))
+    for _ in range(args.warmup):
+        one_step(m)
+    t0 = time.perf_counter()
+    kind = None
+    for _ in range(args.steps):
+        kind = one_step(m)
+    elapsed = time.perf_counter() - t0
+    bytes_step = sum(2 * m * b / 8 for (_, _, _, _, b) in streams)
+    gbs = bytes_step * args.steps / elapsed / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": gbs, "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f80 (long double)",
+        "data": "synthetic",
+        "config": config_of(args, world, desc, n_full),
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": kind,
+                         "sample": f"{m} values per format per step ({len(streams)} formats), "
+                                   f"host decode + compensated long-double DOT"},
+        "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_of(args, world, desc, n_full):
+    n = args.n or n_full
+    return {"workload": f"{desc}; N={n} per GPU", "n_per_gpu": n,
+            "formats": [f for f, _ in WORKLOADS[args.workload][1]],
+            "layout": "dense", "accumulator": args.accum,
+            "l2": "inputs larger than L2 (every pair > 126 MB; consecutive DOTs read different buffers)",
+            "parallelism": f"contiguous shards x{world}, one FP64 all-reduce per step"}
+
+
+# ---- our arm ---------------------------------------------------------------------
+def main():
+    args = parse()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        return run_reference_arm(args, rank, world)
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from accessor_universal_test_b200 import _lib, vectors
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    desc, fmts, layout, n_full = WORKLOADS[args.workload]
+    n = args.n or n_full
+    accum = _lib.ACC_FP32 if args.accum == "fp32" else _lib.ACC_FP64
+    if any(f == "fp64" for f, _ in fmts):
+        accum = _lib.ACC_FP64
+    ws = _lib.Workspace(local)
+    stream = torch.cuda.current_stream().cuda_stream
+    fids, inputs, packed_bytes = [], [], []
+    for name, kind in fmts:
+        fid = _lib.format_id(name)
+        ws.prepare(fid)
+        x = vectors.encoded(ws, fid, layout, kind, SEED, 0, n, first=rank * n)
+        y = vectors.encoded(ws, fid, layout, kind, SEED, 1, n, first=rank * n)
+        fids.append(fid)
+        inputs.append((x, y))
+        packed_bytes.append(2 * n * _lib.format_info(fid)[1] / 8)
+    results = torch.zeros(len(fmts), dtype=torch.float64, device="cuda")
+    res_ptr = results.data_ptr()
+    torch.cuda.synchronize()
+
+    def step():
+        for k, fid in enumerate(fids):
+            x, y = inputs[k]
+            ws.dot(fid, layout, accum, x.data_ptr(), y.data_ptr(), n, res_ptr + 8 * k, stream)
+        if world > 1:
+            dist.all_reduce(results)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(physical_gpu(local)) as clocks:
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(args.steps):
+            step()
+        stop.record()
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(stop)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    step_bytes = sum(packed_bytes) * world
+    value = step_bytes * args.steps / (ms / 1e3) / 1e9
+    elems = 2 * n * len(fmts) * world * args.steps / (ms / 1e3)
+
+    # per-kernel CUDA-event timing (same stream) for the roofline
+    per_kernel = []
+    reps = 20
+    for k, fid in enumerate(fids):
+        x, y = inputs[k]
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            ws.dot(fid, layout, accum, x.data_ptr(), y.data_ptr(), n, res_ptr + 8 * k, stream)
+        b.record()
+        torch.cuda.synchronize()
+        t_ms = a.elapsed_time(b) / reps
+        per_kernel.append((fmts[k][0], t_ms, packed_bytes[k] / (t_ms / 1e3) / 1e9))
+    peak, peak_kind = measured_peak()
+    dom = max(per_kernel, key=lambda r: r[1])
+    traffic = committed_traffic().get(dom[0])
+    if traffic is not None and "bytes_per_value_pair" in traffic:
+        traffic = traffic["bytes_per_value_pair"] * n
+    elif traffic is not None:
+        traffic = traffic.get("bytes_per_launch")
+
+    # e2e through the C ABI from pinned host buffers
+    host_in = [(x.cpu().pin_memory(), y.cpu().pin_memory()) for x, y in inputs]
+    host_out = torch.zeros(len(fmts), dtype=torch.float64).pin_memory()
+    h2d = sum(hx.numel() + hy.numel() for hx, hy in host_in)
+
+    def e2e_step():
+        for k, fid in enumerate(fids):
+            x, y = inputs[k]
+            x.copy_(host_in[k][0], non_blocking=True)
+            y.copy_(host_in[k][1], non_blocking=True)
+            ws.dot(fid, layout, accum, x.data_ptr(), y.data_ptr(), n, res_ptr + 8 * k, stream)
+        if world > 1:
+            dist.all_reduce(results)
+        host_out.copy_(results, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    b.record()
+    torch.cuda.synchronize()
+    e2e_ms = a.elapsed_time(b) / args.e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = step_bytes / (e2e_ms / 1e3) / 1e9
+
+    # CPU baseline + normalised error (rank 0 at N=1): the reference's CPU path
+    # over the full workload on all host cores.
+    cpu_baseline, errors = None, {}
+    gpu_results = host_out.numpy().copy()
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        threads = host_threads()
+        tot_bytes, tot_s, kinds = 0.0, 0.0, set()
+        for k, (name, _) in enumerate(fmts):
+            x, y = inputs[k]
+            xw = x.cpu().numpy().view(np.uint32)
+            yw = y.cpu().numpy().view(np.uint32)
+            stride = 64 if name == "fp64" else _lib.format_info(fids[k])[1]
+            t0 = time.perf_counter()
+            d, s, kind = cpu_reference_dot(name, stride, xw, yw, n, threads)
+            tot_s += time.perf_counter() - t0
+            tot_bytes += packed_bytes[k]
+            kinds.add(kind)
+            ref = np.longdouble(d[0]) + np.longdouble(d[1])
+            sabs = np.longdouble(s[0]) + np.longdouble(s[1])
+            errors[name] = float(abs(np.longdouble(gpu_results[k]) - ref) / sabs) if sabs else 0.0
+        cpu_baseline = {"value": tot_bytes / tot_s / 1e9, "unit": "GB/s", "cores": threads,
+                        "kind": "reference" if kinds == {"reference"} else "port",
+                        "sample": f"the full workload ({len(fmts)} DOTs x {n} values), "
+                                  "host decode + compensated long-double DOT"}
+
+    clk = clocks.summary()
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 products, f64 carry" if accum == _lib.ACC_FP32 else "f64",
+        "data": "synthetic (seeded splitmix64, generated and encoded on the GPU)",
+        "config": config_of(args, world, desc, n_full),
+        "decoded_elems_per_s": elems,
+        "pct_of_8tbs": value / world / 8000.0 * 100.0,
+        "per_format": [{"format": f, "ms": t, "gbs": g, "frac_of_peak": g / peak}
+                       for f, t, g in per_kernel],
+        "normalized_error": errors or None,
+        "roofline": {"bound": "hbm", "kernel": f"dot_kernel[{dom[0]}]", "achieved": dom[2],
+                     "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
+                     "frac": dom[2] / peak, "traffic": traffic},
+        "cpu_baseline": cpu_baseline,
+        "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": 8 * len(fmts)},
+        "gpu_launches": len(fmts) * args.steps,
+        "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"],
+                   "reasons": clk["reasons"]},
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    ws.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

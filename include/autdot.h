@@ -1,0 +1,181 @@
+/*
+ * autdot.h -- C ABI of the B200 decode-fused DOT library (libautdot.so).
+ *
+ * The reference (accessor_universal_test) exposes its DOT path as header-only
+ * C++ templates driven by benchmark CLIs; it has no FFI layer.  This header
+ * is the boundary a binding (ctypes, cgo, JNI, N-API) or the C++ wrappers in
+ * include/aut/ call.  Each entry point names the reference interface it
+ * replaces.  Conventions:
+ *   - plain integers, pointers and sizes only; no C++ or torch types;
+ *   - device pointers are CUDA global memory on the workspace's device;
+ *   - every device call is asynchronous and ordered on `stream`
+ *     (a cudaStream_t passed as void*; NULL = legacy default stream);
+ *   - the return value is a status code; aut_last_error() gives the
+ *     message of the calling thread's last failure (the reference throws
+ *     std::runtime_error from CUDA_CHECK, src/bitwidth_strategy_bench.cu:32-47).
+ */
+#ifndef AUTDOT_H_
+#define AUTDOT_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AUTDOT_ABI_VERSION 1
+
+typedef int32_t aut_status;
+enum {
+  AUT_OK = 0,
+  AUT_ERR_INVALID_ARGUMENT = 1, /* bad pointer, size, enum value       */
+  AUT_ERR_UNSUPPORTED = 2,      /* no kernel for format/layout/accum   */
+  AUT_ERR_CUDA = 3,             /* a CUDA runtime call failed          */
+  AUT_ERR_TOO_LARGE = 4,        /* size beyond a documented maximum    */
+  AUT_ERR_NO_DEVICE = 5         /* no usable CUDA device / wrong arch  */
+};
+
+/* Format families (runtime descriptor of a storage format). */
+enum {
+  AUT_FAMILY_BINARY = 0,      /* storage::binary_format<T,E,finite>        */
+  AUT_FAMILY_FP64_PREFIX = 1, /* storage::fp64_prefix<F>                   */
+  AUT_FAMILY_LNS = 2,         /* lns::format<B,R>; exponent_bits holds R   */
+  AUT_FAMILY_RAW_FP32 = 3,    /* IEEE binary32 storage                     */
+  AUT_FAMILY_RAW_FP64 = 4     /* IEEE binary64 storage                     */
+};
+
+/* Format ids with a decode-fused DOT kernel.  Every other registered format
+ * (storage_formats.hpp:110-262, lns_benchmark_core.hpp:44-61) has an id from
+ * aut_format_id() and host/device codecs, but no DOT kernel yet. */
+enum {
+  AUT_FMT_FP32 = 0,      /* raw binary32                                  */
+  AUT_FMT_FP64 = 1,      /* raw binary64                                  */
+  AUT_FMT_E2M3 = 2,      /* FP6 E2M3, finite (storage_formats.hpp:132)    */
+  AUT_FMT_E8M0 = 3,      /* 9-bit E8 (storage_formats.hpp:161)            */
+  AUT_FMT_E8M1 = 4,      /* 10-bit E8 (:165)                              */
+  AUT_FMT_E8M3 = 5,      /* 12-bit E8 (:170)                              */
+  AUT_FMT_E8M5 = 6,      /* 14-bit E8 (:174)                              */
+  AUT_FMT_BF16_E8M7 = 7, /* 16-bit E8 (cuda_storage_formats.cuh:37-43)    */
+  AUT_FMT_E8M15 = 8,     /* 24-bit E8 (:203)                              */
+  AUT_FMT_LNS8_R3 = 9,   /* lns_benchmark_core.hpp:48                     */
+  AUT_FMT_LNS16_R11 = 10 /* lns_benchmark_core.hpp:56                     */
+};
+
+/* Storage layouts (bitwidth_benchmark_core.hpp:23).
+ * DENSE:  value i at bits [B*i, B*i+B) of little-endian uint32 words, plus
+ *         one zero guard word: aut_storage_bytes() = 4*(ceil(n*B/32)+1).
+ * PADDED: one code per uint8/uint16/uint32 container (storage_type_t). */
+enum { AUT_LAYOUT_DENSE = 0, AUT_LAYOUT_PADDED = 1 };
+
+/* Per-thread accumulator of the fused DOT (compute_kind, :22).  Block and
+ * grid reductions are FP64 for both; FP32 partial sums are carried into
+ * FP64 at least every 128 products. */
+enum { AUT_ACCUM_FP32 = 0, AUT_ACCUM_FP64 = 1 };
+
+/* Decode target type. */
+enum { AUT_TARGET_FP32 = 0, AUT_TARGET_FP64 = 1 };
+
+/* Synthetic generators for aut_generate (seeded, counter based, identical
+ * on host and device for every index). */
+enum {
+  AUT_GEN_SIGNED_UNIT_F64 = 0, /* uniform [-1,1), 2^-51 grid (dot_bench.cu:389-393) */
+  AUT_GEN_SIGNED_UNIT_F32 = 1, /* uniform [-1,1), 2^-22 grid (dot_dataset.hpp:149-153) */
+  AUT_GEN_NORMAL = 2,          /* Irwin-Hall(12) - 6, approximately N(0,1)   */
+  AUT_GEN_LNS_CANCEL = 3       /* vector 0: x ~ U[-1,1); vector 1:
+                                  y_i = s_i x_i (1 + 1e-6 u_i), s alternating */
+};
+
+/* ---- library / format registry ---------------------------------------- */
+const char *aut_version(void);
+int32_t aut_abi_version(void);
+/* Message of the calling thread's last failed call ("" if none). */
+const char *aut_last_error(void);
+
+int32_t aut_format_count(void);
+/* Id of a format by its reference name ("e2m3", "bf16_e8m7", "lns16_r11",
+ * "fp32", ...); -1 when unknown. */
+int32_t aut_format_id(const char *name);
+const char *aut_format_name(int32_t format);
+aut_status aut_format_info(int32_t format, int32_t *family,
+                           int32_t *total_bits, int32_t *exponent_bits,
+                           int32_t *finite);
+/* 1 when aut_dot has a fused kernel for this combination, else 0. */
+int32_t aut_dot_supported(int32_t format, int32_t layout, int32_t accum);
+/* Bytes a caller allocates for n values (dense: includes the guard word;
+ * replaces dense_word_count/dense_data_bytes, bitwidth_benchmark_core.hpp:160-169). */
+uint64_t aut_storage_bytes(int32_t format, int32_t layout, uint64_t n);
+/* Algorithmic (packed) bytes of n values: n * total_bits / 8. */
+double aut_packed_bytes(int32_t format, uint64_t n);
+
+/* ---- workspace: per-device scratch and decode tables ------------------- */
+typedef struct aut_workspace aut_workspace;
+/* Allocates the grid-reduction scratch and binds the library to `device`.
+ * Replaces the reference's partials/result buffers
+ * (src/bitwidth_strategy_bench.cu:466, device_buffer<value_type> partials_(512)). */
+aut_status aut_workspace_create(int32_t device, aut_workspace **out);
+aut_status aut_workspace_destroy(aut_workspace *ws);
+/* Builds (once) the decode tables of `format` so that later calls issue no
+ * host-to-device copies; call before capturing aut_dot in a CUDA graph. */
+aut_status aut_workspace_prepare(aut_workspace *ws, int32_t format);
+/* Number of SMs and the maximum grid the DOT kernels launch on them. */
+aut_status aut_workspace_info(const aut_workspace *ws, int32_t *sm_count,
+                              int32_t *max_blocks);
+
+/* ---- the decode-fused DOT ---------------------------------------------- */
+/* result[0] = sum_i decode(x_i) * decode(y_i), written to device memory.
+ * Replaces dot_thread_kernel + finalize_dot_kernel
+ * (bitwidth_benchmark_kernels.cuh:403-457), the LNS dot_thread_kernel
+ * (lns_benchmark_kernels.cuh:80-131), raw_dot_kernel (:681-703) and the
+ * accessor DOT (src/accessor_dot_bench.cu:417-474) in one call: one launch,
+ * single-pass grid reduction, deterministic for a given device.
+ * x and y hold n values in `layout`; 16-byte aligned pointers take the
+ * vectorised path.  n = 0 writes 0. */
+aut_status aut_dot(aut_workspace *ws, int32_t format, int32_t layout,
+                   int32_t accum, const void *x, const void *y, uint64_t n,
+                   double *result, void *stream);
+
+/* `batch` independent DOTs in one launch: pair b reads
+ * x + b*batch_stride_bytes and y + b*batch_stride_bytes; results[b]. */
+aut_status aut_dot_batched(aut_workspace *ws, int32_t format, int32_t layout,
+                           int32_t accum, const void *x, const void *y,
+                           uint64_t n, uint32_t batch,
+                           uint64_t batch_stride_bytes, double *results,
+                           void *stream);
+
+/* ---- device codecs ------------------------------------------------------ */
+/* out[i] = decode(codes[i]) as float or double, bit-identical to the
+ * reference's host storage::decode / lns::decode (validate_decode_kernel,
+ * lns_benchmark_kernels.cuh:359-374). */
+aut_status aut_decode(aut_workspace *ws, int32_t format, int32_t layout,
+                      int32_t target, const void *codes, uint64_t n,
+                      void *out, void *stream);
+/* Round-to-nearest-even encode of device doubles into `layout`
+ * (encode_padded_kernel + pack_dense_kernel,
+ * bitwidth_benchmark_kernels.cuh:625-668; lns_benchmark_kernels.cuh:309-357).
+ * `codes` must hold aut_storage_bytes(format, layout, n) bytes.  LNS codes
+ * equal the host encoder's for every input (threshold tables built from the
+ * host log2). */
+aut_status aut_encode(aut_workspace *ws, int32_t format, int32_t layout,
+                      const double *values, uint64_t n, void *codes,
+                      void *stream);
+/* out[i] = generator value of index first + i. */
+aut_status aut_generate(int32_t kind, uint64_t seed, int32_t vector_id,
+                        uint64_t first, uint64_t n, double *out, void *stream);
+
+/* ---- host codecs (the host half of storage::encode/decode) -------------- */
+aut_status aut_encode_host(int32_t format, const double *values, uint64_t n,
+                           uint32_t *codes);
+aut_status aut_decode_host(int32_t format, const uint32_t *codes, uint64_t n,
+                           double *out);
+/* Pack codes (one per uint32) into `layout`; out holds aut_storage_bytes(). */
+aut_status aut_pack_host(int32_t format, int32_t layout, const uint32_t *codes,
+                         uint64_t n, void *out);
+aut_status aut_unpack_host(int32_t format, int32_t layout, const void *packed,
+                           uint64_t n, uint32_t *codes);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AUTDOT_H_ */

@@ -1,0 +1,161 @@
+"""The fused DOT through the C ABI against the compensated long-double oracle."""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+from gpu_util import (DOT_FORMATS, SEED, TOL, device_pair, gpu_dot, kind_of,
+                      normalized_error, oracle_codes, oracle_dot)
+
+pytestmark = pytest.mark.gpu
+
+SIZES = [1, 7, 100, 4099, 65536 + 13, (1 << 20) + 37]
+
+
+def _accums(name):
+    return [1] if name == "fp64" else [0, 1]
+
+
+@pytest.mark.parametrize("name", DOT_FORMATS)
+@pytest.mark.parametrize("layout", [0, 1])
+def test_dot_matches_oracle(ws, orc, name, layout):
+    for n in SIZES:
+        x, y = device_pair(ws, name, layout, n)
+        ref_dot, ref_abs = oracle_dot(orc, name, n)
+        for accum in _accums(name):
+            got = gpu_dot(ws, name, layout, accum, x, y, n)
+            err = normalized_error(got, ref_dot, ref_abs)
+            assert err <= TOL[accum], (name, layout, accum, n, got, float(ref_dot), float(err))
+            if name == "e2m3":
+                # products k_a k_b / 64 and their partial sums are exact:
+                # the DOT is the exact sum rounded once
+                assert got == float(ref_dot), (name, n, got, float(ref_dot))
+
+
+def _fnv_words(words):
+    h = 1469598103934665603
+    for w in words.astype(np.uint64).tolist():
+        h ^= w
+        h = (h * 1099511628211) & 0xFFFFFFFFFFFFFFFF
+    return f"0x{h:016x}"
+
+
+def test_dot_matches_reference_golden_vectors(ws):
+    """The reference's own CPU DOT of the same workloads (tests/golden)."""
+    from accessor_universal_test_b200 import _lib
+    golden = json.load(open(os.path.join(GOLDEN, "dot_vectors.json")))
+    assert golden["seed"] == SEED
+    for case in golden["cases"]:
+        name, n = case["format"], case["n"]
+        x, y = device_pair(ws, name, 0, n)
+        if "x_words_fnv" in case:
+            words = _lib.storage_bytes(_lib.format_id(name), 0, n) // 4
+            xw = x[: 4 * words].cpu().numpy().view(np.uint32)
+            yw = y[: 4 * words].cpu().numpy().view(np.uint32)
+            assert _fnv_words(xw) == case["x_words_fnv"], (name, n)
+            assert _fnv_words(yw) == case["y_words_fnv"], (name, n)
+        ref_dot = np.longdouble(case["dot_hi"]) + np.longdouble(case["dot_lo"])
+        ref_abs = np.longdouble(case["sum_abs_hi"]) + np.longdouble(case["sum_abs_lo"])
+        for accum in _accums(name):
+            got = gpu_dot(ws, name, 0, accum, x, y, n)
+            assert normalized_error(got, ref_dot, ref_abs) <= TOL[accum], (name, n, accum)
+
+
+def test_empty_dot_writes_zero(ws):
+    import torch
+    from accessor_universal_test_b200 import _lib
+    res = torch.full((1,), 7.0, dtype=torch.float64, device="cuda")
+    ws.dot(_lib.format_id("e8m0"), 0, 0, 0, 0, 0, res.data_ptr())
+    torch.cuda.synchronize()
+    assert res.item() == 0.0
+
+
+@pytest.mark.parametrize("name", ["e2m3", "e8m0", "e8m15", "bf16_e8m7", "lns16_r11", "fp32"])
+def test_unaligned_streams_take_the_scalar_path(ws, orc, name):
+    import torch
+    n = 50_003
+    x, y = device_pair(ws, name, 0, n)
+    ref_dot, ref_abs = oracle_dot(orc, name, n)
+    xs = torch.zeros(x.numel() + 16, dtype=torch.uint8, device="cuda")
+    ys = torch.zeros(y.numel() + 16, dtype=torch.uint8, device="cuda")
+    xs[4:4 + x.numel()] = x
+    ys[8:8 + y.numel()] = y
+    for accum in (0, 1):
+        got = gpu_dot(ws, name, 0, accum, xs, ys, n, x_off=4, y_off=8)
+        assert normalized_error(got, ref_dot, ref_abs) <= TOL[accum]
+
+
+@pytest.mark.parametrize("name", ["e8m0", "e8m5", "e8m15", "lns8_r3", "lns16_r11", "e2m3"])
+def test_dot_is_deterministic_and_symmetric(ws, name):
+    n = (1 << 22) + 5
+    x, y = device_pair(ws, name, 0, n)
+    for accum in (0, 1):
+        a = gpu_dot(ws, name, 0, accum, x, y, n)
+        b = gpu_dot(ws, name, 0, accum, x, y, n)
+        c = gpu_dot(ws, name, 0, accum, y, x, n)
+        assert a == b == c, (name, accum, a, b, c)
+
+
+@pytest.mark.parametrize("name", ["e8m1", "bf16_e8m7", "e8m15", "lns8_r3", "lns16_r11"])
+def test_special_codes_propagate_like_the_oracle(ws, orc, name):
+    import torch
+    from accessor_universal_test_b200 import _lib
+    fid = _lib.format_id(name)
+    desc = _lib.format_info(fid)
+    n = 20_000
+    _, _, cx = oracle_codes(orc, name, n, 0)
+    _, _, cy = oracle_codes(orc, name, n, 1)
+    cases = {"inf": orc.encode(desc, [np.inf])[0], "nan": orc.encode(desc, [np.nan])[0]}
+    for label, code in cases.items():
+        for pos in (0, 12_345, n - 1):
+            xx = cx.copy()
+            xx[pos] = code
+            # The compensated reference turns +-inf into NaN (its correction
+            # term computes inf - inf), so classify specials from the plain
+            # sum of oracle-decoded products and use the compensated sum for
+            # finite results only.
+            with np.errstate(invalid="ignore", over="ignore"):
+                prods = orc.decode_f64(desc, xx) * orc.decode_f64(desc, cy)
+                plain = prods.sum()
+                (d, s) = orc.dot_codes(desc, xx, cy, threads=1)
+            want = plain if not np.isfinite(plain) else d[0]
+            xb = np.zeros(_lib.storage_bytes(fid, 0, n), np.uint8)
+            yb = np.zeros(_lib.storage_bytes(fid, 0, n), np.uint8)
+            _lib.check(_lib.load().aut_pack_host(fid, 0, xx.ctypes.data, n, xb.ctypes.data))
+            _lib.check(_lib.load().aut_pack_host(fid, 0, cy.ctypes.data, n, yb.ctypes.data))
+            xt, yt = torch.from_numpy(xb).cuda(), torch.from_numpy(yb).cuda()
+            for accum in (0, 1):
+                got = gpu_dot(ws, name, 0, accum, xt, yt, n)
+                if np.isnan(want):
+                    assert np.isnan(got), (name, label, pos)
+                elif np.isinf(want):
+                    assert got == want, (name, label, pos, got, want)
+                else:
+                    assert abs(got - want) <= TOL[accum] * s[0], (name, label, pos, got, want)
+
+
+@pytest.mark.parametrize("name", ["e8m0", "e2m3", "lns16_r11", "fp32"])
+def test_batched_dots_match_single_dots(ws, orc, name):
+    import torch
+    from accessor_universal_test_b200 import _lib
+    fid = _lib.format_id(name)
+    n, batch = 300_007, 5
+    stride = (_lib.storage_bytes(fid, 0, n) + 255) // 256 * 256
+    xb = torch.zeros(stride * batch, dtype=torch.uint8, device="cuda")
+    yb = torch.zeros(stride * batch, dtype=torch.uint8, device="cuda")
+    singles = []
+    for b in range(batch):
+        x, y = device_pair(ws, name, 0, n, seed=SEED + b)
+        xb[b * stride: b * stride + x.numel()] = x[: min(x.numel(), stride)]
+        yb[b * stride: b * stride + y.numel()] = y[: min(y.numel(), stride)]
+        singles.append((gpu_dot(ws, name, 0, 1, x, y, n), x, y))
+    res = torch.full((batch,), float("nan"), dtype=torch.float64, device="cuda")
+    ws.dot_batched(fid, 0, 1, xb.data_ptr(), yb.data_ptr(), n, batch, stride, res.data_ptr())
+    torch.cuda.synchronize()
+    got = res.cpu().numpy()
+    for b in range(batch):
+        ref_dot, ref_abs = oracle_dot(orc, name, n, seed=SEED + b)
+        assert normalized_error(got[b], ref_dot, ref_abs) <= TOL[1], (b, got[b], singles[b][0])
+        assert abs(got[b] - singles[b][0]) <= 2 * TOL[1] * float(ref_abs)
