@@ -23,6 +23,8 @@ FAMILY_BINARY, FAMILY_PREFIX, FAMILY_LNS, FAMILY_RAW_FP32, FAMILY_RAW_FP64 = ran
 DENSE, PADDED = 0, 1
 ACC_FP32, ACC_FP64 = 0, 1
 TARGET_FP32, TARGET_FP64 = 0, 1
+STRATEGY_AUTO, STRATEGY_LDG, STRATEGY_TMA = 0, 1, 2
+STATUS_WAIT_TIMEOUT = 1
 GEN_SIGNED_UNIT_F64, GEN_SIGNED_UNIT_F32, GEN_NORMAL, GEN_LNS_CANCEL = range(4)
 
 # C signatures: name -> (restype, argtypes)
@@ -44,7 +46,9 @@ SIGNATURES = {
     "aut_workspace_destroy": (_i32, [_vp]),
     "aut_workspace_prepare": (_i32, [_vp, _i32]),
     "aut_workspace_info": (_i32, [_vp, _i32p, _i32p]),
+    "aut_workspace_status": (_i32, [_vp, C.POINTER(_u32), _i32]),
     "aut_dot": (_i32, [_vp, _i32, _i32, _i32, _vp, _vp, _u64, _vp, _vp]),
+    "aut_dot_strategy": (_i32, [_vp, _i32, _i32, _i32, _i32, _vp, _vp, _u64, _vp, _vp]),
     "aut_dot_batched": (_i32, [_vp, _i32, _i32, _i32, _vp, _vp, _u64, _u32, _u64, _vp, _vp]),
     "aut_decode": (_i32, [_vp, _i32, _i32, _i32, _vp, _u64, _vp, _vp]),
     "aut_encode": (_i32, [_vp, _i32, _i32, _vp, _u64, _vp, _vp]),
@@ -131,9 +135,15 @@ class Workspace:
     def prepare(self, fmt: int) -> None:
         check(load().aut_workspace_prepare(self.handle, fmt))
 
-    def dot(self, fmt, layout, accum, x_ptr, y_ptr, n, result_ptr, stream=0) -> None:
-        check(load().aut_dot(self.handle, fmt, layout, accum, x_ptr, y_ptr, n,
-                             result_ptr, stream))
+    def dot(self, fmt, layout, accum, x_ptr, y_ptr, n, result_ptr, stream=0,
+            strategy: int = 0) -> None:
+        check(load().aut_dot_strategy(self.handle, fmt, layout, accum, strategy, x_ptr,
+                                      y_ptr, n, result_ptr, stream))
+
+    def status(self, clear: bool = True) -> int:
+        word = C.c_uint32()
+        check(load().aut_workspace_status(self.handle, C.byref(word), 1 if clear else 0))
+        return word.value
 
     def dot_batched(self, fmt, layout, accum, x_ptr, y_ptr, n, batch, stride_bytes,
                     results_ptr, stream=0) -> None:

@@ -1,13 +1,20 @@
 // dot.cu -- the decode-fused DOT kernels and aut_dot / aut_dot_batched.
 //
-// One persistent kernel per (format, layout, accumulator) does the whole
-// DOT: 128-bit vector loads of both code streams, in-register decode, FMA
-// into per-thread accumulators, a warp-shuffle + shared-memory block sum and
-// a single-pass grid reduction into the device result.  This replaces the
+// One persistent kernel per (format, layout, accumulator, access strategy)
+// does the whole DOT: stream both code vectors, decode in registers, FMA into
+// per-thread accumulators, warp-shuffle + shared-memory block sum and a
+// single-pass grid reduction into the device result.  This replaces the
 // reference's dot_thread_kernel + finalize_dot_kernel pair
 // (bitwidth_benchmark_kernels.cuh:403-457), the LNS dot_thread_kernel
 // (lns_benchmark_kernels.cuh:80-131), raw_dot_kernel (:681-703) and the
 // accessor map-reduce (src/accessor_dot_bench.cu:417-454).
+//
+// Access strategies (the reference's access_method axis,
+// bitwidth_benchmark_core.hpp:24):
+//   LDG -- each thread loads whole 16-byte packets into registers;
+//   TMA -- one thread per block streams contiguous tiles of both vectors into
+//          a shared-memory ring with cp.async.bulk (no multicast) and an
+//          mbarrier per stage; threads decode their units from shared memory.
 #include "dot_device.cuh"
 #include "internal.hpp"
 
@@ -28,12 +35,14 @@ struct dot_params {
   double *partials;       // [gridDim.y][gridDim.x]
   unsigned int *tickets;  // [gridDim.y]
   double *results;        // [gridDim.y]
+  unsigned int *status;   // sticky error bits (AUT_STATUS_*)
 };
 
 // ---------------------------------------------------------------------------
-// Codecs.  Each supplies: kS (bits per stored slot), kU (packets per thread
-// per tile), kTableBytes (dynamic shared memory), prepare(), packet() for a
-// whole packet in registers and scalar() for ragged tails.
+// Codecs.  Each supplies kS (bits per stored slot), kU (LDG packets per thread
+// per tile), kTableBytes (dynamic shared memory), kExactLanes (uses the four
+// float lanes for exact partial sums), prepare(), values<NV>() decoding NV
+// consecutive codes from a word array and scalar() for ragged tails.
 // ---------------------------------------------------------------------------
 
 // IEEE-like formats with an 8-bit exponent (e8m0 ... e8m15, bf16, and raw
@@ -44,15 +53,15 @@ template <int S, int W> struct e8_codec {
   static constexpr int kS = S;
   static constexpr int kU = packet_shape<S>::Q == 1 ? 4 : (S == 24 ? 2 : 1);
   static constexpr int kTableBytes = 0;
+  static constexpr bool kExactLanes = false;
   __device__ static void prepare(const void *, unsigned char *) {}
 
-  template <class Acc>
-  __device__ __forceinline__ static void packet(const uint32_t *xw,
+  template <int NV, class Acc>
+  __device__ __forceinline__ static void values(const uint32_t *xw,
                                                 const uint32_t *yw, Acc &acc,
-                                                const unsigned char *) {
-    constexpr int P = packet_shape<S>::P;
+                                                float *, const unsigned char *) {
 #pragma unroll
-    for (int v = 0; v < P; ++v) {
+    for (int v = 0; v < NV; ++v) {
       const float a = __uint_as_float(field_top<S, W>(xw, v));
       const float b = __uint_as_float(field_top<S, W>(yw, v));
       acc.mac(v, a, b);
@@ -75,14 +84,15 @@ struct f64_codec {
   static constexpr int kS = 64;
   static constexpr int kU = 4;
   static constexpr int kTableBytes = 0;
+  static constexpr bool kExactLanes = false;
   __device__ static void prepare(const void *, unsigned char *) {}
 
-  template <class Acc>
-  __device__ __forceinline__ static void packet(const uint32_t *xw,
+  template <int NV, class Acc>
+  __device__ __forceinline__ static void values(const uint32_t *xw,
                                                 const uint32_t *yw, Acc &acc,
-                                                const unsigned char *) {
+                                                float *, const unsigned char *) {
 #pragma unroll
-    for (int v = 0; v < 2; ++v) {
+    for (int v = 0; v < NV; ++v) {
       const double a = __hiloint2double(static_cast<int>(xw[2 * v + 1]),
                                         static_cast<int>(xw[2 * v]));
       const double b = __hiloint2double(static_cast<int>(yw[2 * v + 1]),
@@ -103,19 +113,20 @@ struct f64_codec {
 
 // FP6 E2M3 (finite).  Four 6-bit codes are spread into the low 6 bits of four
 // bytes, the hardware converts byte pairs to f16x2 exactly, and the
-// mixed-precision FMA multiplies two f16 values exactly into an FP32
-// accumulator.  Every e2m3 value is k/8 with |k| <= 60, so products are
-// multiples of 2^-6 below 57 and an FP32 sum of up to 64 of them is exact:
-// the accumulators are carried into FP64 once per packet, which makes the
-// DOT exact up to its final rounding for both accumulator kinds.
+// mixed-precision FMA multiplies two f16 values exactly into an FP32 lane.
+// Every e2m3 value is k/8 with |k| <= 60, so products are multiples of 2^-6
+// below 57 and an FP32 sum of up to 4096 of them is exact: the lanes are
+// carried into FP64 once per tile, which makes the DOT exact up to its final
+// rounding for both accumulator kinds.
 template <int S> struct e2m3_codec {
   static_assert(S == 6 || S == 8, "dense 6-bit or one code per byte");
   static constexpr int kS = S;
   static constexpr int kU = S == 8 ? 4 : 1;
   static constexpr int kTableBytes = 0;
+  static constexpr bool kExactLanes = true;
   __device__ static void prepare(const void *, unsigned char *) {}
 
-  // Codes 4g .. 4g+3 of the packet, one per byte (low 6 bits).
+  // Codes 4g .. 4g+3 of the word array, one per byte (low 6 bits).
   __device__ __forceinline__ static uint32_t bytes4(const uint32_t *w, int g) {
     if constexpr (S == 8) {
       return w[g] & 0x3f3f3f3fu;
@@ -145,21 +156,19 @@ template <int S> struct e2m3_codec {
         : "r"(x2), "r"(y2));
   }
 
-  template <class Acc>
-  __device__ __forceinline__ static void packet(const uint32_t *xw,
-                                                const uint32_t *yw, Acc &acc,
+  template <int NV, class Acc>
+  __device__ __forceinline__ static void values(const uint32_t *xw,
+                                                const uint32_t *yw, Acc &,
+                                                float *lanes,
                                                 const unsigned char *) {
-    constexpr int G = packet_shape<S>::P / 4;
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    static_assert(NV % 4 == 0, "e2m3 decodes groups of four codes");
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
+    for (int g = 0; g < NV / 4; ++g) {
       const uint32_t bx = bytes4(xw, g);
       const uint32_t by = bytes4(yw, g);
-      fma2(s0, s1, to_f16x2(bx), to_f16x2(by));
-      fma2(s2, s3, to_f16x2(bx >> 16), to_f16x2(by >> 16));
+      fma2(lanes[0], lanes[1], to_f16x2(bx), to_f16x2(by));
+      fma2(lanes[2], lanes[3], to_f16x2(bx >> 16), to_f16x2(by >> 16));
     }
-    acc.add_exact((static_cast<double>(s0) + static_cast<double>(s1)) +
-                  (static_cast<double>(s2) + static_cast<double>(s3)));
   }
 
   __device__ __forceinline__ static float decode1(uint32_t c) {
@@ -178,26 +187,28 @@ template <int S> struct e2m3_codec {
 };
 
 // lns8_r3 (one code per byte): a full 256-entry decode table, replicated
-// once per lane in shared memory (entry e of lane l at word e*32 + l), so
+// once per lane in shared memory (entry e of lane l at element e*32 + l), so
 // that a warp's 32 lookups hit 32 different banks.  Table values come from
 // the host exp2f / exp2 and are the reference's decoded values bit for bit.
 template <typename T> struct lns8_codec {
   static constexpr int kS = 8;
   static constexpr int kU = 4;
   static constexpr int kTableBytes = 256 * 32 * static_cast<int>(sizeof(T));
+  static constexpr bool kExactLanes = false;
   __device__ static void prepare(const void *table, unsigned char *smem) {
     const T *g = static_cast<const T *>(table);
     T *s = reinterpret_cast<T *>(smem);
     for (int e = threadIdx.x; e < 256 * 32; e += kThreads) s[e] = g[e >> 5];
   }
 
-  template <class Acc>
-  __device__ __forceinline__ static void packet(const uint32_t *xw,
+  template <int NV, class Acc>
+  __device__ __forceinline__ static void values(const uint32_t *xw,
                                                 const uint32_t *yw, Acc &acc,
+                                                float *,
                                                 const unsigned char *smem) {
     const T *tab = reinterpret_cast<const T *>(smem) + (threadIdx.x & 31);
 #pragma unroll
-    for (int v = 0; v < 16; ++v) {
+    for (int v = 0; v < NV; ++v) {
       const T a = tab[field_low<8, 8>(xw, v) << 5];
       const T b = tab[field_low<8, 8>(yw, v) << 5];
       if constexpr (sizeof(T) == 4)
@@ -226,6 +237,7 @@ template <typename T> struct lns16_codec {
   static constexpr int kS = 16;
   static constexpr int kU = 4;
   static constexpr int kTableBytes = 2048 * static_cast<int>(sizeof(T));
+  static constexpr bool kExactLanes = false;
   __device__ static void prepare(const void *table, unsigned char *smem) {
     const T *g = static_cast<const T *>(table);
     T *s = reinterpret_cast<T *>(smem);
@@ -254,13 +266,14 @@ template <typename T> struct lns16_codec {
     }
   }
 
-  template <class Acc>
-  __device__ __forceinline__ static void packet(const uint32_t *xw,
+  template <int NV, class Acc>
+  __device__ __forceinline__ static void values(const uint32_t *xw,
                                                 const uint32_t *yw, Acc &acc,
+                                                float *,
                                                 const unsigned char *smem) {
     const T *tab = reinterpret_cast<const T *>(smem);
 #pragma unroll
-    for (int v = 0; v < 8; ++v) {
+    for (int v = 0; v < NV; ++v) {
       const T a = decode(field_low<16, 16>(xw, v), tab);
       const T b = decode(field_low<16, 16>(yw, v), tab);
       if constexpr (sizeof(T) == 4)
@@ -281,13 +294,33 @@ template <typename T> struct lns16_codec {
   }
 };
 
+template <class Codec, class Acc>
+__device__ __forceinline__ void flush_tile(Acc &acc, float *lanes) {
+  if constexpr (Codec::kExactLanes) {
+    acc.add_exact((static_cast<double>(lanes[0]) + static_cast<double>(lanes[1])) +
+                  (static_cast<double>(lanes[2]) + static_cast<double>(lanes[3])));
+    lanes[0] = lanes[1] = lanes[2] = lanes[3] = 0.f;
+  }
+  acc.flush();
+}
+
+template <class Codec, class Acc>
+__device__ __forceinline__ void ragged_tail(const unsigned char *xb,
+                                            const unsigned char *yb,
+                                            uint64_t first, uint64_t n,
+                                            Acc &acc, const unsigned char *smem) {
+  for (uint64_t i = first + static_cast<uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
+       i < n; i += static_cast<uint64_t>(gridDim.x) * kThreads)
+    Codec::scalar(xb, yb, i, acc, smem);
+}
+
 // ---------------------------------------------------------------------------
-// The kernel.
+// LDG strategy: packets of Q 16-byte vectors straight into registers.
 // ---------------------------------------------------------------------------
 template <class Codec, class Acc>
 __global__ void __launch_bounds__(kThreads)
-    dot_kernel(const dot_params p) {
-  extern __shared__ __align__(16) unsigned char smem[];
+    dot_ldg_kernel(const dot_params p) {
+  extern __shared__ __align__(128) unsigned char smem[];
   __shared__ double scratch[kThreads / 32];
   constexpr int S = Codec::kS;
   constexpr int Q = packet_shape<S>::Q;
@@ -305,6 +338,7 @@ __global__ void __launch_bounds__(kThreads)
   }
 
   Acc acc;
+  float lanes[4] = {0.f, 0.f, 0.f, 0.f};
   const uint64_t tiles = p.vector_ok ? (p.n / P) / tile_packets : 0;
   const uint4 *X = reinterpret_cast<const uint4 *>(xb);
   const uint4 *Y = reinterpret_cast<const uint4 *>(yb);
@@ -321,18 +355,175 @@ __global__ void __launch_bounds__(kThreads)
     }
 #pragma unroll
     for (int u = 0; u < U; ++u)
-      Codec::packet(reinterpret_cast<const uint32_t *>(xv[u]),
-                    reinterpret_cast<const uint32_t *>(yv[u]), acc, smem);
-    acc.flush();
+      Codec::template values<P>(reinterpret_cast<const uint32_t *>(xv[u]),
+                                reinterpret_cast<const uint32_t *>(yv[u]), acc,
+                                lanes, smem);
+    flush_tile<Codec>(acc, lanes);
   }
 
-  // Ragged tail (everything when a pointer is not 16-byte aligned).
-  const uint64_t done = tiles * tile_packets * P;
-  for (uint64_t i = done + static_cast<uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
-       i < p.n; i += static_cast<uint64_t>(gridDim.x) * kThreads)
-    Codec::scalar(xb, yb, i, acc, smem);
-
+  ragged_tail<Codec>(xb, yb, tiles * tile_packets * P, p.n, acc, smem);
   const double s = block_sum(acc.value(), scratch);
+  grid_finish(s, p.partials + static_cast<uint64_t>(batch) * gridDim.x,
+              p.tickets + batch, p.results + batch, scratch);
+}
+
+// ---------------------------------------------------------------------------
+// TMA strategy: a shared-memory ring fed by cp.async.bulk.
+// ---------------------------------------------------------------------------
+// Geometry of one tile: every thread owns kValuesPerThread consecutive codes
+// in units of UW words (UW = S / gcd(S, 32) is odd, so a warp reading word k
+// of 32 consecutive units hits 32 different banks).
+template <int S> struct tma_shape {
+  static constexpr int G = gcd_int(S, 32);
+  static constexpr int UW = S / G;                 // words per unit
+  static constexpr int UV = S == 64 ? 1 : 32 / G;  // codes per unit
+  static constexpr int VPT = S >= 24 ? 16 : 32;    // codes per thread per tile
+  static constexpr int V = VPT / UV;               // units per thread per tile
+  static constexpr int TILE_WORDS = kThreads * V * UW;
+  static constexpr int TILE_BYTES = TILE_WORDS * 4;  // per vector
+  static constexpr uint64_t TILE_VALUES = static_cast<uint64_t>(kThreads) * VPT;
+  static constexpr int RING_BYTES = 64 * 1024;
+  static constexpr int STAGES_RAW = RING_BYTES / (2 * TILE_BYTES);
+  static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
+  static_assert(TILE_BYTES % 16 == 0, "bulk copies move 16-byte multiples");
+  static_assert(V * UV == VPT, "units tile the thread's codes");
+};
+
+constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 2 GHz
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(
+                   smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// Returns false when the phase did not complete within kWaitCycles.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  const uint32_t addr = smem_addr(bar);
+  const long long start = clock64();
+  while (true) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if (clock64() - start > kWaitCycles) return false;
+  }
+}
+
+__device__ __forceinline__ void bulk_load(void *dst, const void *src,
+                                          uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1], %2, [%3];" ::"r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+template <class Codec, class Acc>
+__global__ void __launch_bounds__(kThreads)
+    dot_tma_kernel(const dot_params p) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ double scratch[kThreads / 32];
+  using shape = tma_shape<Codec::kS>;
+  constexpr int UW = shape::UW;
+  constexpr int UV = shape::UV;
+  constexpr int V = shape::V;
+  constexpr int STAGES = shape::STAGES;
+  constexpr int TILE_BYTES = shape::TILE_BYTES;
+  __shared__ __align__(8) uint64_t full[STAGES];
+
+  const unsigned int batch = blockIdx.y;
+  const unsigned char *xb = p.x + batch * p.batch_stride;
+  const unsigned char *yb = p.y + batch * p.batch_stride;
+  unsigned char *ring = smem + Codec::kTableBytes;
+
+  const uint64_t tiles = p.vector_ok ? p.n / shape::TILE_VALUES : 0;
+  const uint64_t mine =
+      tiles > blockIdx.x ? (tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+
+  auto issue = [&](uint64_t k) {
+    const uint64_t t = blockIdx.x + k * gridDim.x;
+    unsigned char *dst = ring + (k % STAGES) * (2 * TILE_BYTES);
+    uint64_t *bar = &full[k % STAGES];
+    mbar_expect_tx(bar, 2u * TILE_BYTES);
+    bulk_load(dst, xb + t * TILE_BYTES, TILE_BYTES, bar);
+    bulk_load(dst + TILE_BYTES, yb + t * TILE_BYTES, TILE_BYTES, bar);
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1);
+    mbar_fence_init();
+  }
+  if constexpr (Codec::kTableBytes > 0) Codec::prepare(p.table, smem);
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (uint64_t k = 0; k < mine && k < STAGES; ++k) issue(k);
+
+  Acc acc;
+  float lanes[4] = {0.f, 0.f, 0.f, 0.f};
+  bool failed = false;
+  uint64_t k = 0;
+  for (; k < mine; ++k) {
+    const bool ok = mbar_wait(&full[k % STAGES], static_cast<uint32_t>((k / STAGES) & 1));
+    const uint32_t *xs =
+        reinterpret_cast<const uint32_t *>(ring + (k % STAGES) * (2 * TILE_BYTES));
+    const uint32_t *ys = xs + shape::TILE_WORDS;
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const int u = threadIdx.x + v * kThreads;
+      uint32_t xw[UW], yw[UW];
+#pragma unroll
+      for (int w = 0; w < UW; ++w) {
+        xw[w] = xs[u * UW + w];
+        yw[w] = ys[u * UW + w];
+      }
+      Codec::template values<UV>(xw, yw, acc, lanes, smem);
+    }
+    flush_tile<Codec>(acc, lanes);
+    // Every thread is done with this stage (and the exit decision is the
+    // same for all threads) before it is refilled.
+    if (__syncthreads_or(ok ? 0 : 1)) {
+      failed = true;
+      break;
+    }
+    if (threadIdx.x == 0 && k + STAGES < mine) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(k + STAGES);
+    }
+  }
+  if (failed) {
+    // Let the copies this block still has in flight land before it exits.
+    if (threadIdx.x == 0) {
+      for (uint64_t j = k; j < mine && j < k + STAGES; ++j)
+        mbar_wait(&full[j % STAGES], static_cast<uint32_t>((j / STAGES) & 1));
+      atomicOr(p.status, static_cast<unsigned int>(AUT_STATUS_WAIT_TIMEOUT));
+    }
+    __syncthreads();
+  } else {
+    ragged_tail<Codec>(xb, yb, tiles * shape::TILE_VALUES, p.n, acc, smem);
+  }
+  const double mine_sum = failed ? __longlong_as_double(0x7ff8000000000000ll) : acc.value();
+  const double s = block_sum(mine_sum, scratch);
   grid_finish(s, p.partials + static_cast<uint64_t>(batch) * gridDim.x,
               p.tickets + batch, p.results + batch, scratch);
 }
@@ -350,54 +541,88 @@ using kernel_fn = void (*)(aut::dev::dot_params);
 struct kernel_entry {
   kernel_fn fn = nullptr;
   int smem = 0;
-  int stride = 0;      // bits per stored slot
-  int table_kind = 0;  // 0 none, 1 lns full f32, 2 lns full f64, 3 frac f32, 4 frac f64
-  int packets_per_thread = 1;
+  int stride = 0;       // bits per stored slot
+  int table_kind = 0;   // 0 none, 1 lns full f32, 2 lns full f64, 3 frac f32, 4 frac f64
+  uint64_t tile_values = 0;  // codes per block-tile of the vector path
   int blocks_per_sm = 0;
 };
 
-template <class Codec, class Acc> kernel_entry make_entry(int table_kind) {
+template <class Codec, class Acc>
+kernel_entry make_entry(int strategy, int table_kind) {
   kernel_entry e;
-  e.fn = aut::dev::dot_kernel<Codec, Acc>;
-  e.smem = Codec::kTableBytes;
   e.stride = Codec::kS;
   e.table_kind = table_kind;
-  e.packets_per_thread = Codec::kU;
+  if (strategy == AUT_STRATEGY_TMA) {
+    using shape = aut::dev::tma_shape<Codec::kS>;
+    e.fn = aut::dev::dot_tma_kernel<Codec, Acc>;
+    e.smem = Codec::kTableBytes + shape::STAGES * 2 * shape::TILE_BYTES;
+    e.tile_values = shape::TILE_VALUES;
+  } else {
+    e.fn = aut::dev::dot_ldg_kernel<Codec, Acc>;
+    e.smem = Codec::kTableBytes;
+    e.tile_values = static_cast<uint64_t>(aut::dev::packet_shape<Codec::kS>::P) *
+                    aut::dev::kThreads * Codec::kU;
+  }
   return e;
 }
 
-template <class Codec> kernel_entry pick(int accum, int table_kind) {
-  return accum == AUT_ACCUM_FP32 ? make_entry<Codec, aut::dev::acc_f32>(table_kind)
-                                 : make_entry<Codec, aut::dev::acc_f64>(table_kind);
+template <class Codec>
+kernel_entry pick(int strategy, int accum, int table_kind) {
+  return accum == AUT_ACCUM_FP32
+             ? make_entry<Codec, aut::dev::acc_f32>(strategy, table_kind)
+             : make_entry<Codec, aut::dev::acc_f64>(strategy, table_kind);
 }
 
-kernel_entry lookup(int32_t format, int32_t layout, int32_t accum) {
-  using namespace aut::dev;
-  const bool dense = layout == AUT_LAYOUT_DENSE;
+// The strategy AUTO resolves to per format, chosen from CUDA-event timings
+// of both strategies at N = 2^27 on B200 (packed GB/s, FP32 accumulator):
+//   fp32 6916 LDG / 6636 TMA     fp64  7106 / 7242     e2m3 5140 / 4642
+//   e8m0 4294 / 5529     e8m1 5517 / 5846     e8m3 5841 / 6090
+//   e8m5 4543 / 6377     bf16 6636 / 6519     e8m15 6417 / 6689
+//   lns8_r3 3580 / 3395  lns16_r11 3540 / 3648
+// Packets of several 16-byte vectors (S = 9, 10, 12, 14, 24) load strided
+// per thread and stall on the LSU queue; the bulk-copy ring removes that.
+// Decode-bound formats (e2m3, lns8) lose more to the staging instructions
+// than they gain.
+int auto_strategy(int32_t format, int32_t layout) {
+  (void)layout;
   switch (format) {
-  case AUT_FMT_FP32: return pick<e8_codec<32, 32>>(accum, 0);
+  case AUT_FMT_FP32:
+  case AUT_FMT_E2M3:
+  case AUT_FMT_BF16_E8M7:
+  case AUT_FMT_LNS8_R3: return AUT_STRATEGY_LDG;
+  default: return AUT_STRATEGY_TMA;
+  }
+}
+
+kernel_entry lookup(int32_t format, int32_t layout, int32_t accum, int strategy) {
+  using namespace aut::dev;
+  if (strategy == AUT_STRATEGY_AUTO) strategy = auto_strategy(format, layout);
+  const bool dense = layout == AUT_LAYOUT_DENSE;
+  const int s = strategy;
+  switch (format) {
+  case AUT_FMT_FP32: return pick<e8_codec<32, 32>>(s, accum, 0);
   case AUT_FMT_FP64:
     if (accum != AUT_ACCUM_FP64) return {};
-    return make_entry<f64_codec, acc_f64>(0);
+    return make_entry<f64_codec, acc_f64>(s, 0);
   case AUT_FMT_E2M3:
-    return dense ? pick<e2m3_codec<6>>(accum, 0) : pick<e2m3_codec<8>>(accum, 0);
+    return dense ? pick<e2m3_codec<6>>(s, accum, 0) : pick<e2m3_codec<8>>(s, accum, 0);
   case AUT_FMT_E8M0:
-    return dense ? pick<e8_codec<9, 9>>(accum, 0) : pick<e8_codec<16, 9>>(accum, 0);
+    return dense ? pick<e8_codec<9, 9>>(s, accum, 0) : pick<e8_codec<16, 9>>(s, accum, 0);
   case AUT_FMT_E8M1:
-    return dense ? pick<e8_codec<10, 10>>(accum, 0) : pick<e8_codec<16, 10>>(accum, 0);
+    return dense ? pick<e8_codec<10, 10>>(s, accum, 0) : pick<e8_codec<16, 10>>(s, accum, 0);
   case AUT_FMT_E8M3:
-    return dense ? pick<e8_codec<12, 12>>(accum, 0) : pick<e8_codec<16, 12>>(accum, 0);
+    return dense ? pick<e8_codec<12, 12>>(s, accum, 0) : pick<e8_codec<16, 12>>(s, accum, 0);
   case AUT_FMT_E8M5:
-    return dense ? pick<e8_codec<14, 14>>(accum, 0) : pick<e8_codec<16, 14>>(accum, 0);
-  case AUT_FMT_BF16_E8M7: return pick<e8_codec<16, 16>>(accum, 0);
+    return dense ? pick<e8_codec<14, 14>>(s, accum, 0) : pick<e8_codec<16, 14>>(s, accum, 0);
+  case AUT_FMT_BF16_E8M7: return pick<e8_codec<16, 16>>(s, accum, 0);
   case AUT_FMT_E8M15:
-    return dense ? pick<e8_codec<24, 24>>(accum, 0) : pick<e8_codec<32, 24>>(accum, 0);
+    return dense ? pick<e8_codec<24, 24>>(s, accum, 0) : pick<e8_codec<32, 24>>(s, accum, 0);
   case AUT_FMT_LNS8_R3:
-    return accum == AUT_ACCUM_FP32 ? make_entry<lns8_codec<float>, acc_f32>(1)
-                                   : make_entry<lns8_codec<double>, acc_f64>(2);
+    return accum == AUT_ACCUM_FP32 ? make_entry<lns8_codec<float>, acc_f32>(s, 1)
+                                   : make_entry<lns8_codec<double>, acc_f64>(s, 2);
   case AUT_FMT_LNS16_R11:
-    return accum == AUT_ACCUM_FP32 ? make_entry<lns16_codec<float>, acc_f32>(3)
-                                   : make_entry<lns16_codec<double>, acc_f64>(4);
+    return accum == AUT_ACCUM_FP32 ? make_entry<lns16_codec<float>, acc_f32>(s, 3)
+                                   : make_entry<lns16_codec<double>, acc_f64>(s, 4);
   default: return {};
   }
 }
@@ -405,8 +630,8 @@ kernel_entry lookup(int32_t format, int32_t layout, int32_t accum) {
 // Occupancy of each kernel, cached per function pointer.
 struct occupancy_cache {
   std::mutex mutex;
-  kernel_fn fns[128] = {};
-  int blocks[128] = {};
+  kernel_fn fns[256] = {};
+  int blocks[256] = {};
   int count = 0;
 };
 occupancy_cache &cache() {
@@ -422,7 +647,9 @@ aut_status blocks_per_sm(kernel_entry &e) {
       e.blocks_per_sm = c.blocks[k];
       return AUT_OK;
     }
-  if (e.smem > 48 * 1024)
+  // Dynamic shared memory plus the kernel's static barriers may pass the
+  // 48 KB default even when the dynamic part alone does not.
+  if (e.smem > 0)
     AUT_CUDA_TRY(cudaFuncSetAttribute(reinterpret_cast<const void *>(e.fn),
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       e.smem));
@@ -430,7 +657,7 @@ aut_status blocks_per_sm(kernel_entry &e) {
   AUT_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
       &b, reinterpret_cast<const void *>(e.fn), aut::dev::kThreads, e.smem));
   if (b < 1) return fail(AUT_ERR_UNSUPPORTED, "kernel does not fit on an SM");
-  if (c.count < 128) {
+  if (c.count < 256) {
     c.fns[c.count] = e.fn;
     c.blocks[c.count] = b;
     ++c.count;
@@ -439,30 +666,21 @@ aut_status blocks_per_sm(kernel_entry &e) {
   return AUT_OK;
 }
 
-uint64_t packet_values(int stride) {
-  int g = stride, b = 128;
-  while (b != 0) {
-    const int r = g % b;
-    g = b;
-    b = r;
-  }
-  return static_cast<uint64_t>(128 / g);
-}
-
 } // namespace
 
 int32_t dot_supported(int32_t format, int32_t layout, int32_t accum) {
   if (layout != AUT_LAYOUT_DENSE && layout != AUT_LAYOUT_PADDED) return 0;
   if (accum != AUT_ACCUM_FP32 && accum != AUT_ACCUM_FP64) return 0;
-  return lookup(format, layout, accum).fn != nullptr ? 1 : 0;
+  return lookup(format, layout, accum, AUT_STRATEGY_AUTO).fn != nullptr ? 1 : 0;
 }
 
 aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
-                      int32_t accum, const void *x, const void *y, uint64_t n,
-                      uint32_t batch, uint64_t batch_stride, double *results,
-                      void *stream, double *partials, unsigned int *tickets,
-                      int max_blocks_total) {
-  kernel_entry e = lookup(format, layout, accum);
+                      int32_t accum, int32_t strategy, const void *x,
+                      const void *y, uint64_t n, uint32_t batch,
+                      uint64_t batch_stride, double *results, void *stream,
+                      double *partials, unsigned int *tickets,
+                      unsigned int *status, int max_blocks_total) {
+  kernel_entry e = lookup(format, layout, accum, strategy);
   if (e.fn == nullptr)
     return fail(AUT_ERR_UNSUPPORTED,
                 "no fused DOT kernel for this format/layout/accumulator");
@@ -480,14 +698,11 @@ aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
                                 : static_cast<const void *>(t->frac_f64);
   }
 
-  const uint64_t P = packet_values(e.stride);
-  const uint64_t tile_values =
-      P * aut::dev::kThreads * static_cast<uint64_t>(e.packets_per_thread);
   const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
                        (reinterpret_cast<uintptr_t>(y) % 16 == 0) &&
                        (batch <= 1 || batch_stride % 16 == 0);
   const int cap = ws->sm_count * e.blocks_per_sm;
-  uint64_t wanted = aligned ? (n / tile_values) : 0;
+  uint64_t wanted = aligned ? (n / e.tile_values) : 0;
   if (wanted == 0) wanted = (n + aut::dev::kThreads - 1) / aut::dev::kThreads;
   if (wanted == 0) wanted = 1;
   for (uint32_t b0 = 0; b0 < batch; b0 += kMaxBatchPerLaunch) {
@@ -508,6 +723,7 @@ aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
     p.partials = partials;
     p.tickets = tickets;
     p.results = results + b0;
+    p.status = status;
     dim3 grid(static_cast<unsigned>(per_pair), nb);
     e.fn<<<grid, aut::dev::kThreads, e.smem, static_cast<cudaStream_t>(stream)>>>(p);
     AUT_CUDA_TRY(cudaGetLastError());

@@ -59,7 +59,8 @@ struct aut_workspace {
   int sm_count = 0;
   int max_blocks = 0;       // per launch, all batches together
   double *partials = nullptr; // [kMaxBatchPerLaunch * max_blocks]
-  unsigned int *tickets = nullptr; // [kMaxBatchPerLaunch], kept at zero
+  unsigned int *tickets = nullptr; // [kMaxBatchPerLaunch + 1], kept at zero;
+                                   // the last word is the sticky status
   std::mutex mutex;
   int lns_ids[aut::lib::kLnsFormatsCached] = {-1, -1, -1, -1, -1, -1, -1, -1};
   aut::lib::lns_tables lns[aut::lib::kLnsFormatsCached];

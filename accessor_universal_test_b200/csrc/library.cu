@@ -14,10 +14,11 @@
 namespace aut::lib {
 
 aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
-                      int32_t accum, const void *x, const void *y, uint64_t n,
-                      uint32_t batch, uint64_t batch_stride, double *results,
-                      void *stream, double *partials, unsigned int *tickets,
-                      int max_blocks_total);
+                      int32_t accum, int32_t strategy, const void *x,
+                      const void *y, uint64_t n, uint32_t batch,
+                      uint64_t batch_stride, double *results, void *stream,
+                      double *partials, unsigned int *tickets,
+                      unsigned int *status, int max_blocks_total);
 int32_t dot_supported(int32_t format, int32_t layout, int32_t accum);
 
 // ---- format registry ----------------------------------------------------------
@@ -436,9 +437,10 @@ aut_status aut_workspace_create(int32_t device, aut_workspace **out) {
   ws->sm_count = prop.multiProcessorCount;
   ws->max_blocks = prop.multiProcessorCount * (prop.maxThreadsPerMultiProcessor / 256);
   const size_t np = static_cast<size_t>(kMaxBatchPerLaunch) * ws->max_blocks;
+  const size_t nt = static_cast<size_t>(kMaxBatchPerLaunch) + 1;
   cudaError_t e = cudaMalloc(&ws->partials, np * sizeof(double));
-  if (e == cudaSuccess) e = cudaMalloc(&ws->tickets, kMaxBatchPerLaunch * sizeof(unsigned int));
-  if (e == cudaSuccess) e = cudaMemset(ws->tickets, 0, kMaxBatchPerLaunch * sizeof(unsigned int));
+  if (e == cudaSuccess) e = cudaMalloc(&ws->tickets, nt * sizeof(unsigned int));
+  if (e == cudaSuccess) e = cudaMemset(ws->tickets, 0, nt * sizeof(unsigned int));
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
     cudaFree(ws->partials);
@@ -483,6 +485,23 @@ aut_status aut_workspace_info(const aut_workspace *ws, int32_t *sm_count,
   return AUT_OK;
 }
 
+aut_status aut_workspace_status(aut_workspace *ws, uint32_t *status,
+                                int32_t clear) {
+  clear_error();
+  if (ws == nullptr || status == nullptr)
+    return fail(AUT_ERR_INVALID_ARGUMENT, "workspace or status is NULL");
+  device_scope scope(ws->device);
+  AUT_CUDA_TRY(scope.err);
+  AUT_CUDA_TRY(cudaDeviceSynchronize());
+  unsigned int word = 0;
+  AUT_CUDA_TRY(cudaMemcpy(&word, ws->tickets + kMaxBatchPerLaunch, sizeof word,
+                          cudaMemcpyDeviceToHost));
+  *status = word;
+  if (clear && word != 0)
+    AUT_CUDA_TRY(cudaMemset(ws->tickets + kMaxBatchPerLaunch, 0, sizeof word));
+  return AUT_OK;
+}
+
 static aut_status check_dot_args(aut_workspace *ws, int32_t format,
                                  int32_t layout, int32_t accum, const void *x,
                                  const void *y, uint64_t n, const double *res) {
@@ -505,13 +524,24 @@ static aut_status check_dot_args(aut_workspace *ws, int32_t format,
 aut_status aut_dot(aut_workspace *ws, int32_t format, int32_t layout,
                    int32_t accum, const void *x, const void *y, uint64_t n,
                    double *result, void *stream) {
+  return aut_dot_strategy(ws, format, layout, accum, AUT_STRATEGY_AUTO, x, y,
+                          n, result, stream);
+}
+
+aut_status aut_dot_strategy(aut_workspace *ws, int32_t format, int32_t layout,
+                            int32_t accum, int32_t strategy, const void *x,
+                            const void *y, uint64_t n, double *result,
+                            void *stream) {
   clear_error();
   aut_status st = check_dot_args(ws, format, layout, accum, x, y, n, result);
   if (st != AUT_OK) return st;
+  if (strategy < AUT_STRATEGY_AUTO || strategy > AUT_STRATEGY_TMA)
+    return fail(AUT_ERR_INVALID_ARGUMENT, "unknown access strategy");
   device_scope scope(ws->device);
   AUT_CUDA_TRY(scope.err);
-  return dot_launch(ws, format, layout, accum, x, y, n, 1, 0, result, stream,
-                    ws->partials, ws->tickets, ws->max_blocks);
+  return dot_launch(ws, format, layout, accum, strategy, x, y, n, 1, 0, result,
+                    stream, ws->partials, ws->tickets,
+                    ws->tickets + kMaxBatchPerLaunch, ws->max_blocks);
 }
 
 aut_status aut_dot_batched(aut_workspace *ws, int32_t format, int32_t layout,
@@ -527,9 +557,10 @@ aut_status aut_dot_batched(aut_workspace *ws, int32_t format, int32_t layout,
     return fail(AUT_ERR_INVALID_ARGUMENT, "batch stride smaller than one vector");
   device_scope scope(ws->device);
   AUT_CUDA_TRY(scope.err);
-  return dot_launch(ws, format, layout, accum, x, y, n, batch,
-                    batch_stride_bytes, results, stream, ws->partials,
-                    ws->tickets, ws->max_blocks);
+  return dot_launch(ws, format, layout, accum, AUT_STRATEGY_AUTO, x, y, n,
+                    batch, batch_stride_bytes, results, stream, ws->partials,
+                    ws->tickets, ws->tickets + kMaxBatchPerLaunch,
+                    ws->max_blocks);
 }
 
 aut_status aut_decode(aut_workspace *ws, int32_t format, int32_t layout,

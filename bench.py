@@ -64,6 +64,7 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="e8-sweep")
     p.add_argument("--accum", choices=["fp32", "fp64"], default="fp32")
+    p.add_argument("--strategy", choices=["auto", "ldg", "tma"], default="auto")
     p.add_argument("--n", type=int, default=0, help="values per GPU (default: workload's)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--e2e-steps", type=int, default=6)
@@ -292,6 +293,7 @@ def main():
     if any(f == "fp64" for f, _ in fmts):
         accum = _lib.ACC_FP64
     ws = _lib.Workspace(local)
+    strategy = {"auto": 0, "ldg": 1, "tma": 2}[args.strategy]
     stream = torch.cuda.current_stream().cuda_stream
     fids, inputs, packed_bytes = [], [], []
     for name, kind in fmts:
@@ -309,7 +311,8 @@ def main():
     def step():
         for k, fid in enumerate(fids):
             x, y = inputs[k]
-            ws.dot(fid, layout, accum, x.data_ptr(), y.data_ptr(), n, res_ptr + 8 * k, stream)
+            ws.dot(fid, layout, accum, x.data_ptr(), y.data_ptr(), n, res_ptr + 8 * k, stream,
+                   strategy)
         if world > 1:
             dist.all_reduce(results)
 
@@ -335,19 +338,29 @@ def main():
     value = step_bytes * args.steps / (ms / 1e3) / 1e9
     elems = 2 * n * len(fmts) * world * args.steps / (ms / 1e3)
 
-    # per-kernel CUDA-event timing (same stream) for the roofline
-    per_kernel = []
+    # per-kernel CUDA-event timing (same stream) for the roofline, for the
+    # strategy in use and for each explicit access strategy
     reps = 20
-    for k, fid in enumerate(fids):
+
+    def time_kernel(k, strat):
         x, y = inputs[k]
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for _ in range(reps):
-            ws.dot(fid, layout, accum, x.data_ptr(), y.data_ptr(), n, res_ptr + 8 * k, stream)
+            ws.dot(fids[k], layout, accum, x.data_ptr(), y.data_ptr(), n, res_ptr + 8 * k,
+                   stream, strat)
         b.record()
         torch.cuda.synchronize()
-        t_ms = a.elapsed_time(b) / reps
+        return a.elapsed_time(b) / reps
+
+    per_kernel, by_strategy = [], {}
+    for k, fid in enumerate(fids):
+        t_ms = time_kernel(k, strategy)
         per_kernel.append((fmts[k][0], t_ms, packed_bytes[k] / (t_ms / 1e3) / 1e9))
+        by_strategy[fmts[k][0]] = {name: packed_bytes[k] / (time_kernel(k, s) / 1e3) / 1e9
+                                   for name, s in (("ldg", 1), ("tma", 2))}
+    if ws.status() != 0:
+        raise RuntimeError("a bounded device wait timed out during the benchmark")
     peak, peak_kind = measured_peak()
     dom = max(per_kernel, key=lambda r: r[1])
     traffic = committed_traffic().get(dom[0])
@@ -366,7 +379,8 @@ def main():
             x, y = inputs[k]
             x.copy_(host_in[k][0], non_blocking=True)
             y.copy_(host_in[k][1], non_blocking=True)
-            ws.dot(fid, layout, accum, x.data_ptr(), y.data_ptr(), n, res_ptr + 8 * k, stream)
+            ws.dot(fid, layout, accum, x.data_ptr(), y.data_ptr(), n, res_ptr + 8 * k, stream,
+                   strategy)
         if world > 1:
             dist.all_reduce(results)
         host_out.copy_(results, non_blocking=True)
@@ -424,8 +438,10 @@ def main():
         "config": config_of(args, world, desc, n_full),
         "decoded_elems_per_s": elems,
         "pct_of_8tbs": value / world / 8000.0 * 100.0,
-        "per_format": [{"format": f, "ms": t, "gbs": g, "frac_of_peak": g / peak}
+        "per_format": [{"format": f, "ms": t, "gbs": g, "frac_of_peak": g / peak,
+                        "gbs_by_strategy": by_strategy[f]}
                        for f, t, g in per_kernel],
+        "strategy": args.strategy,
         "normalized_error": errors or None,
         "roofline": {"bound": "hbm", "kernel": f"dot_kernel[{dom[0]}]", "achieved": dom[2],
                      "peak": peak, "peak_source": peak_kind, "unit": "GB/s",

@@ -76,6 +76,20 @@ enum { AUT_ACCUM_FP32 = 0, AUT_ACCUM_FP64 = 1 };
 /* Decode target type. */
 enum { AUT_TARGET_FP32 = 0, AUT_TARGET_FP64 = 1 };
 
+/* How the fused DOT streams its operands (access_method,
+ * bitwidth_benchmark_core.hpp:24).  AUTO picks the measured best per format. */
+enum {
+  AUT_STRATEGY_AUTO = 0,
+  AUT_STRATEGY_LDG = 1, /* 16-byte vector loads straight into registers   */
+  AUT_STRATEGY_TMA = 2  /* cp.async.bulk tiles into a shared-memory ring   */
+};
+
+/* Sticky device status bits reported by aut_workspace_status(). */
+enum {
+  AUT_STATUS_WAIT_TIMEOUT = 1 /* a bounded pipeline wait gave up; the
+                                 affected results were written as NaN */
+};
+
 /* Synthetic generators for aut_generate (seeded, counter based, identical
  * on host and device for every index). */
 enum {
@@ -121,6 +135,10 @@ aut_status aut_workspace_prepare(aut_workspace *ws, int32_t format);
 /* Number of SMs and the maximum grid the DOT kernels launch on them. */
 aut_status aut_workspace_info(const aut_workspace *ws, int32_t *sm_count,
                               int32_t *max_blocks);
+/* Waits for the device, then reports (and with clear != 0 resets) the
+ * sticky AUT_STATUS_* bits the kernels of this workspace raised. */
+aut_status aut_workspace_status(aut_workspace *ws, uint32_t *status,
+                                int32_t clear);
 
 /* ---- the decode-fused DOT ---------------------------------------------- */
 /* result[0] = sum_i decode(x_i) * decode(y_i), written to device memory.
@@ -134,6 +152,13 @@ aut_status aut_workspace_info(const aut_workspace *ws, int32_t *sm_count,
 aut_status aut_dot(aut_workspace *ws, int32_t format, int32_t layout,
                    int32_t accum, const void *x, const void *y, uint64_t n,
                    double *result, void *stream);
+
+/* aut_dot with an explicit access strategy (AUT_STRATEGY_*), the axis the
+ * reference's strategy benchmarks sweep (src/bitwidth_strategy_bench.cu:704-742). */
+aut_status aut_dot_strategy(aut_workspace *ws, int32_t format, int32_t layout,
+                            int32_t accum, int32_t strategy, const void *x,
+                            const void *y, uint64_t n, double *result,
+                            void *stream);
 
 /* `batch` independent DOTs in one launch: pair b reads
  * x + b*batch_stride_bytes and y + b*batch_stride_bytes; results[b]. */

@@ -6,8 +6,8 @@ import numpy as np
 import pytest
 
 from conftest import GOLDEN
-from gpu_util import (DOT_FORMATS, SEED, TOL, device_pair, gpu_dot, kind_of,
-                      normalized_error, oracle_codes, oracle_dot)
+from gpu_util import (DOT_FORMATS, SEED, STRATEGIES, TOL, device_pair, gpu_dot,
+                      kind_of, normalized_error, oracle_codes, oracle_dot)
 
 pytestmark = pytest.mark.gpu
 
@@ -20,12 +20,13 @@ def _accums(name):
 
 @pytest.mark.parametrize("name", DOT_FORMATS)
 @pytest.mark.parametrize("layout", [0, 1])
-def test_dot_matches_oracle(ws, orc, name, layout):
+@pytest.mark.parametrize("strategy", STRATEGIES)
+def test_dot_matches_oracle(ws, orc, name, layout, strategy):
     for n in SIZES:
         x, y = device_pair(ws, name, layout, n)
         ref_dot, ref_abs = oracle_dot(orc, name, n)
         for accum in _accums(name):
-            got = gpu_dot(ws, name, layout, accum, x, y, n)
+            got = gpu_dot(ws, name, layout, accum, x, y, n, strategy=strategy)
             err = normalized_error(got, ref_dot, ref_abs)
             assert err <= TOL[accum], (name, layout, accum, n, got, float(ref_dot), float(err))
             if name == "e2m3":
@@ -88,13 +89,14 @@ def test_unaligned_streams_take_the_scalar_path(ws, orc, name):
 
 
 @pytest.mark.parametrize("name", ["e8m0", "e8m5", "e8m15", "lns8_r3", "lns16_r11", "e2m3"])
-def test_dot_is_deterministic_and_symmetric(ws, name):
+@pytest.mark.parametrize("strategy", STRATEGIES)
+def test_dot_is_deterministic_and_symmetric(ws, name, strategy):
     n = (1 << 22) + 5
     x, y = device_pair(ws, name, 0, n)
     for accum in (0, 1):
-        a = gpu_dot(ws, name, 0, accum, x, y, n)
-        b = gpu_dot(ws, name, 0, accum, x, y, n)
-        c = gpu_dot(ws, name, 0, accum, y, x, n)
+        a = gpu_dot(ws, name, 0, accum, x, y, n, strategy=strategy)
+        b = gpu_dot(ws, name, 0, accum, x, y, n, strategy=strategy)
+        c = gpu_dot(ws, name, 0, accum, y, x, n, strategy=strategy)
         assert a == b == c, (name, accum, a, b, c)
 
 
