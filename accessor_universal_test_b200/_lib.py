@@ -50,6 +50,7 @@ SIGNATURES = {
     "aut_dot": (_i32, [_vp, _i32, _i32, _i32, _vp, _vp, _u64, _vp, _vp]),
     "aut_dot_strategy": (_i32, [_vp, _i32, _i32, _i32, _i32, _vp, _vp, _u64, _vp, _vp]),
     "aut_dot_batched": (_i32, [_vp, _i32, _i32, _i32, _vp, _vp, _u64, _u32, _u64, _vp, _vp]),
+    "aut_dot_noalloc": (_i32, [_i32, _i32, _i32, _vp, _vp, _u64, _u32, _u64, _vp, _vp]),
     "aut_decode": (_i32, [_vp, _i32, _i32, _i32, _vp, _u64, _vp, _vp]),
     "aut_encode": (_i32, [_vp, _i32, _i32, _vp, _u64, _vp, _vp]),
     "aut_generate": (_i32, [_i32, _u64, _i32, _u64, _u64, _vp, _vp]),

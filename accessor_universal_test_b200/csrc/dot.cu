@@ -731,4 +731,52 @@ aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
   return AUT_OK;
 }
 
+// Same launch as dot_launch for callers that bring their own reduction
+// scratch and have no workspace: formats that need decode tables (LNS) are
+// refused, the grid never uses more than `slots` partial slots in total, and
+// nothing is allocated.
+aut_status dot_launch_scratch(int sm_count, int32_t format, int32_t layout,
+                              int32_t accum, const void *x, const void *y,
+                              uint64_t n, uint32_t batch, uint64_t batch_stride,
+                              double *results, void *stream, double *partials,
+                              unsigned int *tickets, unsigned int *status,
+                              int slots) {
+  kernel_entry e = lookup(format, layout, accum, AUT_STRATEGY_AUTO);
+  if (e.fn == nullptr)
+    return fail(AUT_ERR_UNSUPPORTED,
+                "no fused DOT kernel for this format/layout/accumulator");
+  if (e.table_kind != 0)
+    return fail(AUT_ERR_UNSUPPORTED,
+                "this format decodes through tables kept in a workspace; use aut_dot");
+  aut_status st = blocks_per_sm(e);
+  if (st != AUT_OK) return st;
+  const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(y) % 16 == 0) &&
+                       (batch <= 1 || batch_stride % 16 == 0);
+  uint64_t wanted = aligned ? (n / e.tile_values) : 0;
+  if (wanted == 0) wanted = (n + aut::dev::kThreads - 1) / aut::dev::kThreads;
+  if (wanted == 0) wanted = 1;
+  int per_pair = (sm_count * e.blocks_per_sm + static_cast<int>(batch) - 1) /
+                 static_cast<int>(batch);
+  const int cap = slots / static_cast<int>(batch);
+  if (per_pair > cap) per_pair = cap;
+  if (static_cast<uint64_t>(per_pair) > wanted) per_pair = static_cast<int>(wanted);
+  if (per_pair < 1) per_pair = 1;
+  aut::dev::dot_params p;
+  p.x = static_cast<const unsigned char *>(x);
+  p.y = static_cast<const unsigned char *>(y);
+  p.n = n;
+  p.batch_stride = batch_stride;
+  p.vector_ok = aligned ? 1 : 0;
+  p.table = nullptr;
+  p.partials = partials;
+  p.tickets = tickets;
+  p.results = results;
+  p.status = status;
+  dim3 grid(static_cast<unsigned>(per_pair), batch);
+  e.fn<<<grid, aut::dev::kThreads, e.smem, static_cast<cudaStream_t>(stream)>>>(p);
+  AUT_CUDA_TRY(cudaGetLastError());
+  return AUT_OK;
+}
+
 } // namespace aut::lib

@@ -168,6 +168,23 @@ aut_status aut_dot_batched(aut_workspace *ws, int32_t format, int32_t layout,
                            uint64_t batch_stride_bytes, double *results,
                            void *stream);
 
+/* The fused DOT without a workspace, for callers that cannot allocate device
+ * memory (a host framework that owns the GPU's memory through its own pool,
+ * a latency-critical path that cannot absorb cudaMalloc's device-wide
+ * synchronisation, a foreign-language caller with nowhere to keep a
+ * workspace).  No counterpart in the reference: it always allocates its
+ * partials with cudaMalloc.  The reduction scratch is a fixed 32 KiB device
+ * array inside the library (held on every GPU that loads it until exit):
+ * at most 64 DOTs per call (batch > 64 -> AUT_ERR_TOO_LARGE); table-decoded
+ * formats (LNS) -> AUT_ERR_UNSUPPORTED.  All calls share that array, so
+ * calls that overlap on one GPU race; serialise them.  The first call on a
+ * device looks up the array's address; make it before any stream capture.
+ * Arguments as in aut_dot_batched, on the calling thread's current device. */
+aut_status aut_dot_noalloc(int32_t format, int32_t layout, int32_t accum,
+                           const void *x, const void *y, uint64_t n,
+                           uint32_t batch, uint64_t batch_stride_bytes,
+                           double *results, void *stream);
+
 /* ---- device codecs ------------------------------------------------------ */
 /* out[i] = decode(codes[i]) as float or double, bit-identical to the
  * reference's host storage::decode / lns::decode (validate_decode_kernel,
