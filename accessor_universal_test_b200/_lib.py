@@ -23,9 +23,9 @@ FAMILY_BINARY, FAMILY_PREFIX, FAMILY_LNS, FAMILY_RAW_FP32, FAMILY_RAW_FP64 = ran
 DENSE, PADDED = 0, 1
 ACC_FP32, ACC_FP64 = 0, 1
 TARGET_FP32, TARGET_FP64 = 0, 1
-STRATEGY_AUTO, STRATEGY_LDG, STRATEGY_TMA = 0, 1, 2
+STRATEGY_AUTO, STRATEGY_LDG, STRATEGY_TMA, STRATEGY_SCALAR = 0, 1, 2, 3
 STATUS_WAIT_TIMEOUT = 1
-GEN_SIGNED_UNIT_F64, GEN_SIGNED_UNIT_F32, GEN_NORMAL, GEN_LNS_CANCEL = range(4)
+GEN_SIGNED_UNIT_F64, GEN_SIGNED_UNIT_F32, GEN_NORMAL, GEN_LNS_CANCEL, GEN_POSITIVE_UNIT_F64 = range(5)
 
 # C signatures: name -> (restype, argtypes)
 _i32, _u32, _u64, _dbl = C.c_int32, C.c_uint32, C.c_uint64, C.c_double

@@ -87,8 +87,9 @@ def build_tools() -> list[str]:
         exe = os.path.join(LIB_DIR, os.path.splitext(os.path.basename(src))[0])
         if _stale(exe, [src, LIB] + _headers()):
             cmd = ["g++", "-O2", "-std=c++17", f"-I{INCLUDE}", "-I/usr/local/cuda/include",
-                   src, "-o", exe, f"-L{LIB_DIR}", "-lautdot", f"-Wl,-rpath,{LIB_DIR}",
-                   "-Wl,-rpath,$ORIGIN", "-L/usr/local/cuda/lib64", "-lcudart", "-lpthread"]
+                   src, "-o", exe, f"-L{LIB_DIR}", "-lautdot",
+                   "-Wl,-rpath,$ORIGIN", "-L/usr/local/cuda/lib64", "-lcublas", "-lcudart",
+                   "-lpthread"]
             r = subprocess.run(cmd, capture_output=True, text=True)
             if r.returncode != 0:
                 raise RuntimeError(f"g++ failed on {src}:\n{r.stdout}\n{r.stderr}")

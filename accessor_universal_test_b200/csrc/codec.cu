@@ -204,6 +204,8 @@ __device__ __forceinline__ double synthetic(int kind, uint64_t seed,
     for (uint64_t k = 0; k < 12; ++k) acc += splitmix64((i * 12u + k) ^ ls) >> 11;
     return __dsub_rn(__dmul_rn(__ull2double_rn(acc), 0x1p-53), 6.0);
   }
+  case AUT_GEN_POSITIVE_UNIT_F64:
+    return __dmul_rn(__ull2double_rn((splitmix64(i ^ ls) >> 11) + 1u), 0x1p-53);
   default: {  // AUT_GEN_LNS_CANCEL
     const double x = signed_unit_f64(splitmix64(i ^ lane_seed(seed, 0)));
     if (vector_id == 0) return x;

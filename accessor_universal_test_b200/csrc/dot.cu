@@ -680,7 +680,11 @@ aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
                       uint64_t batch_stride, double *results, void *stream,
                       double *partials, unsigned int *tickets,
                       unsigned int *status, int max_blocks_total) {
-  kernel_entry e = lookup(format, layout, accum, strategy);
+  // SCALAR runs the LDG kernel with the vector path switched off, so every
+  // code goes through the per-value load and decode.
+  const bool scalar_only = strategy == AUT_STRATEGY_SCALAR;
+  kernel_entry e = lookup(format, layout, accum,
+                          scalar_only ? AUT_STRATEGY_LDG : strategy);
   if (e.fn == nullptr)
     return fail(AUT_ERR_UNSUPPORTED,
                 "no fused DOT kernel for this format/layout/accumulator");
@@ -698,7 +702,8 @@ aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
                                 : static_cast<const void *>(t->frac_f64);
   }
 
-  const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+  const bool aligned = !scalar_only &&
+                       (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
                        (reinterpret_cast<uintptr_t>(y) % 16 == 0) &&
                        (batch <= 1 || batch_stride % 16 == 0);
   const int cap = ws->sm_count * e.blocks_per_sm;

@@ -535,7 +535,7 @@ aut_status aut_dot_strategy(aut_workspace *ws, int32_t format, int32_t layout,
   clear_error();
   aut_status st = check_dot_args(ws, format, layout, accum, x, y, n, result);
   if (st != AUT_OK) return st;
-  if (strategy < AUT_STRATEGY_AUTO || strategy > AUT_STRATEGY_TMA)
+  if (strategy < AUT_STRATEGY_AUTO || strategy > AUT_STRATEGY_SCALAR)
     return fail(AUT_ERR_INVALID_ARGUMENT, "unknown access strategy");
   device_scope scope(ws->device);
   AUT_CUDA_TRY(scope.err);
@@ -602,7 +602,7 @@ aut_status aut_encode(aut_workspace *ws, int32_t format, int32_t layout,
 aut_status aut_generate(int32_t kind, uint64_t seed, int32_t vector_id,
                         uint64_t first, uint64_t n, double *out, void *stream) {
   clear_error();
-  if (kind < AUT_GEN_SIGNED_UNIT_F64 || kind > AUT_GEN_LNS_CANCEL)
+  if (kind < AUT_GEN_SIGNED_UNIT_F64 || kind > AUT_GEN_POSITIVE_UNIT_F64)
     return fail(AUT_ERR_INVALID_ARGUMENT, "unknown generator kind");
   if (n > 0 && out == nullptr) return fail(AUT_ERR_INVALID_ARGUMENT, "out is NULL");
   return launch_generate(kind, seed, vector_id, first, n, out,

@@ -1,0 +1,318 @@
+// strategy_bench -- the reference's strategy benchmarks on libautdot.
+//
+// Flags and CSV schemas of src/bitwidth_strategy_bench.cu (options :76-153,
+// header :448-453) and src/lns_strategy_bench.cu (options :80-160, header
+// :626-633), so the reference's validators and summarisers read the output
+// unchanged.  Differences: formats are chosen at run time (--formats) instead
+// of one binary per width, the access strategies are this library's
+// (scalar / thread_packet = LDG / tma_bulk = TMA), data come from the seeded
+// generators of aut_generate (uniform_0_1: (0,1]; normal_0_1: Irwin-Hall)
+// instead of cuRAND, and GEMV rows are not produced (--gemv-* are accepted).
+#include <autdot.h>
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <ctime>
+#include <fstream>
+#include <iomanip>
+#include <iostream>
+#include <set>
+#include <sstream>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+namespace {
+
+void cuda_check(cudaError_t e, const char *what) {
+  if (e != cudaSuccess)
+    throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+void aut_check(aut_status s, const char *what) {
+  if (s != AUT_OK)
+    throw std::runtime_error(std::string(what) + ": " + aut_last_error());
+}
+
+std::vector<std::string> split(const std::string &text) {
+  std::vector<std::string> out;
+  std::stringstream ss(text);
+  std::string tok;
+  while (std::getline(ss, tok, ','))
+    if (!tok.empty()) out.push_back(tok);
+  return out;
+}
+
+struct options {
+  std::string family{"bitwidth"};
+  std::vector<std::string> formats;
+  std::string mode{"screen"};
+  std::vector<int> dot_powers{24};
+  std::vector<std::string> distributions{"uniform_0_1", "normal_0_1"};
+  std::vector<std::string> accums{"fp32", "fp64"};
+  int warmup{5};
+  int samples{3};
+  double target_sample_ms{10.0};
+  uint64_t seed{0x243f6a8885a308d3ull};
+  std::string output;
+  std::set<std::string> variants;
+};
+
+options parse(int argc, char **argv) {
+  options o;
+  for (int i = 1; i < argc; ++i) {
+    const std::string a = argv[i];
+    auto value = [&]() -> std::string {
+      if (++i >= argc) throw std::runtime_error("missing value after " + a);
+      return argv[i];
+    };
+    if (a == "--family") o.family = value();
+    else if (a == "--formats") o.formats = split(value());
+    else if (a == "--mode") o.mode = value();
+    else if (a == "--dot-powers") {
+      o.dot_powers.clear();
+      for (auto &t : split(value())) o.dot_powers.push_back(std::stoi(t));
+    } else if (a == "--gemv-powers" || a == "--gemv-rows") value();
+    else if (a == "--distributions") o.distributions = split(value());
+    else if (a == "--accums") o.accums = split(value());
+    else if (a == "--warmup") o.warmup = std::stoi(value());
+    else if (a == "--samples") o.samples = std::stoi(value());
+    else if (a == "--target-sample-ms") o.target_sample_ms = std::stod(value());
+    else if (a == "--seed") o.seed = std::stoull(value(), nullptr, 0);
+    else if (a == "--output") o.output = value();
+    else if (a == "--variants") for (auto &t : split(value())) o.variants.insert(t);
+    else if (a == "--variant-file") {
+      std::ifstream in(value());
+      if (!in) throw std::runtime_error("cannot open variant file");
+      std::string line;
+      while (std::getline(in, line))
+        if (!line.empty() && line[0] != '#') o.variants.insert(line);
+    } else if (a == "--help" || a == "-h") {
+      std::cout << "strategy_bench --family bitwidth|lns --formats e2m3,e8m0,... "
+                   "--mode smoke|screen|full --dot-powers 24 --distributions "
+                   "uniform_0_1,normal_0_1 --accums fp32,fp64 --warmup N --samples N "
+                   "--target-sample-ms X --seed N --output PATH [--variants a,b] "
+                   "[--variant-file PATH]\n";
+      std::exit(0);
+    } else throw std::runtime_error("unknown option: " + a);
+  }
+  if (o.family != "bitwidth" && o.family != "lns")
+    throw std::runtime_error("--family must be bitwidth or lns");
+  if (o.formats.empty())
+    o.formats = o.family == "lns" ? std::vector<std::string>{"lns8_r3", "lns16_r11"}
+                                  : std::vector<std::string>{"e2m3", "e8m0", "e8m1", "e8m3",
+                                                             "e8m5", "bf16_e8m7", "e8m15"};
+  if (o.output.empty())
+    o.output = o.family == "lns" ? "lns_timing_samples.csv" : "timing_samples.csv";
+  if (o.mode == "smoke") {  // the reference's smoke overrides
+    o.dot_powers = {12};
+    o.warmup = 1;
+    o.samples = 1;
+    o.target_sample_ms = 0.0;
+  }
+  return o;
+}
+
+std::string utc_now() {
+  const auto t = std::chrono::system_clock::to_time_t(std::chrono::system_clock::now());
+  std::tm utc{};
+  gmtime_r(&t, &utc);
+  std::ostringstream s;
+  s << std::put_time(&utc, "%Y-%m-%dT%H:%M:%SZ");
+  return s.str();
+}
+
+struct device_buffer {
+  void *p = nullptr;
+  explicit device_buffer(size_t bytes) { cuda_check(cudaMalloc(&p, bytes < 16 ? 16 : bytes), "cudaMalloc"); }
+  ~device_buffer() { cudaFree(p); }
+  device_buffer(const device_buffer &) = delete;
+  device_buffer &operator=(const device_buffer &) = delete;
+};
+
+int gcd_int(int a, int b) { return b == 0 ? a : gcd_int(b, a % b); }
+
+struct access {
+  const char *name;     // access_method column
+  int32_t strategy;
+  const char *redistribution;
+};
+
+const char *decoder_name(const std::string &family, const std::string &fmt, bool scalar) {
+  if (scalar) return family == "lns" ? "reference_exp2" : "generic";
+  if (fmt == "e2m3") return "native_packed";
+  if (fmt == "lns8_r3") return "full_lut_shared";
+  if (fmt == "lns16_r11") return "fraction_lut_shared";
+  return "direct_shift";
+}
+
+} // namespace
+
+int main(int argc, char **argv) {
+  try {
+    const options o = parse(argc, argv);
+    cudaDeviceProp prop{};
+    cuda_check(cudaGetDeviceProperties(&prop, 0), "cudaGetDeviceProperties");
+    aut_workspace *ws = nullptr;
+    aut_check(aut_workspace_create(0, &ws), "aut_workspace_create");
+    std::cout << "Strategy benchmark (" << o.family << "): GPU " << prop.name << " (sm_"
+              << prop.major << prop.minor << ")\n";
+
+    std::ifstream existing(o.output, std::ios::binary | std::ios::ate);
+    const bool header = !existing || existing.tellg() == 0;
+    existing.close();
+    std::ofstream csv(o.output, std::ios::app);
+    if (!csv) throw std::runtime_error("cannot open output: " + o.output);
+    if (header) {
+      if (o.family == "lns")
+        csv << "timestamp,gpu,mode,distribution,kernel,number_family,format,bits,"
+               "log_integer_bits,log_fraction_bits,arithmetic_type,multiply_method,"
+               "storage_layout,access_method,packet_values,load_word_bits,loader_threads,"
+               "consumer_threads,values_per_consumer,redistribution,decoder,strategy_id,"
+               "N,M,rows,logical_input_bytes,physical_input_bytes,table_bytes,blocks,"
+               "threads,warmup,sample,iterations,total_ms,mean_ms,result,valid\n";
+      else
+        csv << "timestamp,gpu,mode,distribution,kernel,format,bits,exponent_bits,"
+               "mantissa_bits,arithmetic_type,storage_layout,access_method,packet_values,"
+               "load_word_bits,loader_threads,consumer_threads,values_per_consumer,"
+               "redistribution,decoder,strategy_id,N,M,rows,logical_input_bytes,"
+               "physical_input_bytes,table_bytes,blocks,threads,warmup,sample,iterations,"
+               "total_ms,mean_ms,result,valid\n";
+    }
+    const std::string stamp = utc_now();
+    int32_t sm = 0, max_blocks = 0;
+    aut_workspace_info(ws, &sm, &max_blocks);
+
+    cudaEvent_t start, stop;
+    cuda_check(cudaEventCreate(&start), "event");
+    cuda_check(cudaEventCreate(&stop), "event");
+    double *d_result = nullptr;
+    cuda_check(cudaMalloc(&d_result, sizeof(double)), "cudaMalloc");
+
+    const access accesses[] = {{"scalar", AUT_STRATEGY_SCALAR, "none"},
+                               {"thread_packet", AUT_STRATEGY_LDG, "none"},
+                               {"tma_bulk", AUT_STRATEGY_TMA, "tma_bulk_shared"}};
+    const int max_power = *std::max_element(o.dot_powers.begin(), o.dot_powers.end());
+    const uint64_t max_n = uint64_t{1} << max_power;
+    device_buffer values(max_n * sizeof(double));
+
+    for (size_t d = 0; d < o.distributions.size(); ++d) {
+      const std::string &dist = o.distributions[d];
+      const int32_t kind = dist == "uniform_0_1"  ? AUT_GEN_POSITIVE_UNIT_F64
+                           : dist == "normal_0_1" ? AUT_GEN_NORMAL
+                                                  : -1;
+      if (kind < 0) throw std::runtime_error("unsupported distribution: " + dist);
+      const uint64_t seed = o.seed + d * 0x9e3779b97f4a7c15ull;
+      std::cout << dist << "\n";
+      for (const auto &name : o.formats) {
+        const int32_t fid = aut_format_id(name.c_str());
+        if (fid < 0) throw std::runtime_error("unknown format: " + name);
+        int32_t family = 0, bits = 0, ebits = 0, finite = 0;
+        aut_format_info(fid, &family, &bits, &ebits, &finite);
+        aut_check(aut_workspace_prepare(ws, fid), "aut_workspace_prepare");
+        for (const auto &acc_name : o.accums) {
+          const int32_t accum = acc_name == "fp64" ? AUT_ACCUM_FP64 : AUT_ACCUM_FP32;
+          std::cout << "  " << name << " -> " << acc_name << "\n";
+          for (int32_t layout : {AUT_LAYOUT_DENSE, AUT_LAYOUT_PADDED}) {
+            if (!aut_dot_supported(fid, layout, accum)) continue;
+            const int stride = layout == AUT_LAYOUT_DENSE ? bits
+                               : bits <= 8 ? 8 : bits <= 16 ? 16 : 32;
+            for (int power : o.dot_powers) {
+              const uint64_t n = uint64_t{1} << power;
+              device_buffer xs(aut_storage_bytes(fid, layout, n));
+              device_buffer ys(aut_storage_bytes(fid, layout, n));
+              aut_check(aut_generate(kind, seed, 0, 0, n, static_cast<double *>(values.p), nullptr), "generate");
+              aut_check(aut_encode(ws, fid, layout, static_cast<double *>(values.p), n, xs.p, nullptr), "encode");
+              aut_check(aut_generate(kind, seed, 1, 0, n, static_cast<double *>(values.p), nullptr), "generate");
+              aut_check(aut_encode(ws, fid, layout, static_cast<double *>(values.p), n, ys.p, nullptr), "encode");
+              cuda_check(cudaDeviceSynchronize(), "encode");
+              for (const access &ac : accesses) {
+                const bool scalar = ac.strategy == AUT_STRATEGY_SCALAR;
+                const char *dec = decoder_name(o.family, name, scalar);
+                const int packet = scalar ? 1
+                                   : ac.strategy == AUT_STRATEGY_LDG
+                                       ? 128 * (stride / gcd_int(stride, 128)) / stride
+                                       : (stride >= 24 ? 16 : 32);
+                std::ostringstream id;
+                if (o.family == "lns") id << "ordinary/";
+                id << (layout == AUT_LAYOUT_DENSE ? "dense" : "padded") << '/' << ac.name
+                   << "/x" << packet << '/' << dec;
+                const std::string qualified = name + "/" + acc_name + "/" + id.str();
+                if (!o.variants.empty() && !o.variants.count(id.str()) &&
+                    !o.variants.count(qualified))
+                  continue;
+                auto launch = [&] {
+                  aut_check(aut_dot_strategy(ws, fid, layout, accum, ac.strategy, xs.p, ys.p, n,
+                                             d_result, nullptr),
+                            "aut_dot_strategy");
+                };
+                auto timed = [&](int iters) {
+                  cuda_check(cudaEventRecord(start), "record");
+                  for (int k = 0; k < iters; ++k) launch();
+                  cuda_check(cudaEventRecord(stop), "record");
+                  cuda_check(cudaEventSynchronize(stop), "sync");
+                  float ms = 0.f;
+                  cuda_check(cudaEventElapsedTime(&ms, start, stop), "elapsed");
+                  return static_cast<double>(ms);
+                };
+                for (int w = 0; w < o.warmup; ++w) launch();
+                cuda_check(cudaDeviceSynchronize(), "warmup");
+                const double pilot = timed(1);
+                int iterations = 1;
+                if (o.target_sample_ms > 0 && pilot > 0)
+                  iterations = std::clamp(static_cast<int>(std::ceil(o.target_sample_ms / pilot)), 1, 10000);
+                std::vector<double> times;
+                for (int s = 0; s < o.samples; ++s) times.push_back(timed(iterations));
+                double result = 0.0;
+                cuda_check(cudaMemcpy(&result, d_result, sizeof result, cudaMemcpyDeviceToHost), "copy");
+                uint32_t status = 0;
+                aut_check(aut_workspace_status(ws, &status, 1), "status");
+                const int valid = std::isfinite(result) && status == 0 ? 1 : 0;
+                const double logical = 2.0 * n * bits / 8.0;
+                const uint64_t physical = 2 * (layout == AUT_LAYOUT_DENSE
+                                                   ? (n * bits + 7) / 8
+                                                   : n * (stride / 8));
+                const int table = name == "lns8_r3" ? 256 * (accum == AUT_ACCUM_FP64 ? 8 : 4)
+                                  : name == "lns16_r11" ? 2048 * (accum == AUT_ACCUM_FP64 ? 8 : 4)
+                                                        : 0;
+                for (size_t s = 0; s < times.size(); ++s) {
+                  csv << stamp << ',' << prop.name << ',' << o.mode << ',' << dist << ",dot,";
+                  if (o.family == "lns")
+                    csv << "lns," << name << ',' << bits << ',' << (bits - 1 - ebits) << ','
+                        << ebits << ',' << acc_name << ",ordinary,";
+                  else
+                    csv << name << ',' << bits << ',' << ebits << ',' << (bits - 1 - ebits)
+                        << ',' << acc_name << ',';
+                  csv << (layout == AUT_LAYOUT_DENSE ? "dense" : "padded") << ',' << ac.name
+                      << ',' << packet << ',' << (layout == AUT_LAYOUT_DENSE ? 32 : stride)
+                      << ',' << (ac.strategy == AUT_STRATEGY_TMA ? 1 : 1) << ','
+                      << (ac.strategy == AUT_STRATEGY_TMA ? 256 : 1) << ',' << packet << ','
+                      << ac.redistribution << ',' << dec << ',' << id.str() << ',' << n
+                      << ",0,1," << logical << ',' << physical << ',' << table << ','
+                      << max_blocks << ",256," << o.warmup << ',' << s << ',' << iterations
+                      << ',' << times[s] << ',' << times[s] / iterations << ','
+                      << std::setprecision(17) << result << std::setprecision(6) << ','
+                      << valid << '\n';
+                }
+                if (o.mode == "smoke") std::cout << "    " << qualified << "\n";
+              }
+            }
+          }
+        }
+      }
+    }
+    csv.flush();
+    cudaFree(d_result);
+    aut_workspace_destroy(ws);
+    std::cout << "Wrote " << o.output << "\n";
+    return 0;
+  } catch (const std::exception &e) {
+    std::cerr << "error: " << e.what() << "\n";
+    return 1;
+  }
+}

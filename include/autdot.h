@@ -80,8 +80,10 @@ enum { AUT_TARGET_FP32 = 0, AUT_TARGET_FP64 = 1 };
  * bitwidth_benchmark_core.hpp:24).  AUTO picks the measured best per format. */
 enum {
   AUT_STRATEGY_AUTO = 0,
-  AUT_STRATEGY_LDG = 1, /* 16-byte vector loads straight into registers   */
-  AUT_STRATEGY_TMA = 2  /* cp.async.bulk tiles into a shared-memory ring   */
+  AUT_STRATEGY_LDG = 1,   /* 16-byte vector loads straight into registers   */
+  AUT_STRATEGY_TMA = 2,   /* cp.async.bulk tiles into a shared-memory ring   */
+  AUT_STRATEGY_SCALAR = 3 /* one code per load (the reference's scalar
+                             access method); the slow baseline            */
 };
 
 /* Sticky device status bits reported by aut_workspace_status(). */
@@ -96,8 +98,9 @@ enum {
   AUT_GEN_SIGNED_UNIT_F64 = 0, /* uniform [-1,1), 2^-51 grid (dot_bench.cu:389-393) */
   AUT_GEN_SIGNED_UNIT_F32 = 1, /* uniform [-1,1), 2^-22 grid (dot_dataset.hpp:149-153) */
   AUT_GEN_NORMAL = 2,          /* Irwin-Hall(12) - 6, approximately N(0,1)   */
-  AUT_GEN_LNS_CANCEL = 3       /* vector 0: x ~ U[-1,1); vector 1:
+  AUT_GEN_LNS_CANCEL = 3,      /* vector 0: x ~ U[-1,1); vector 1:
                                   y_i = s_i x_i (1 + 1e-6 u_i), s alternating */
+  AUT_GEN_POSITIVE_UNIT_F64 = 4 /* uniform (0,1], 2^-53 grid (dot_bench.cu:375-379) */
 };
 
 /* ---- library / format registry ---------------------------------------- */

@@ -471,6 +471,8 @@ double orc_synthetic_value(int kind, uint64_t seed, int vector_id,
     const double p = x * scale;
     return (index & 1u) ? -p : p;
   }
+  case 4: /* positive_unit<double>, dot_bench.cu:375-379 */
+    return (double)((orc_splitmix64(index ^ ls) >> 11) + 1u) * 0x1p-53;
   default:
     return NAN;
   }

@@ -77,11 +77,12 @@ void orc_dot_v1_fill(int kind, uint64_t seed, int parameter, int vector_id,
 uint64_t orc_fnv1a_f32(const float *values, uint64_t count);
 
 /* Synthetic workload generators shared with the device generator
- * (accessor_universal_test_b200/csrc/generate.cuh).  kind:
+ * (accessor_universal_test_b200/csrc/codec.cu).  kind:
  *   0 = signed uniform double in [-1,1) (dot_bench.cu:389-393 mapping)
  *   1 = signed uniform float  in [-1,1) (dot_dataset.hpp:149-153 mapping)
  *   2 = approximately N(0,1): Irwin-Hall sum of 12 uniforms minus 6
  *   3 = LNS cancellation partner: y_i = s_i * x_i * (1 + 1e-6 u_i)
+ *   4 = positive uniform double in (0,1] (dot_bench.cu:375-379 mapping)
  */
 double orc_synthetic_value(int kind, uint64_t seed, int vector_id,
                            uint64_t index);

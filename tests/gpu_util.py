@@ -30,7 +30,7 @@ def device_pair(ws, name, layout, n, seed=SEED):
     return x, y
 
 
-STRATEGIES = [1, 2]  # LDG (registers), TMA (bulk copies into shared memory)
+STRATEGIES = [1, 2, 3]  # LDG (registers), TMA (bulk copies into shared memory), SCALAR
 
 
 def gpu_dot(ws, name, layout, accum, x, y, n, x_off=0, y_off=0, strategy=0):

@@ -98,7 +98,7 @@ def test_device_encode_matches_host_encoder(ws, orc, name, layout):
         raise AssertionError(f"{name}: {vals[bad]} -> {back[bad]} want {want_codes[bad]}")
 
 
-@pytest.mark.parametrize("kind", [0, 1, 2, 3])
+@pytest.mark.parametrize("kind", [0, 1, 2, 3, 4])
 def test_device_generators_match_oracle(orc, autlib, kind):
     import torch
     from accessor_universal_test_b200 import _lib
