@@ -13,7 +13,8 @@
 // bitwidth_benchmark_core.hpp:24):
 //   LDG -- each thread loads whole 16-byte packets into registers;
 //   TMA -- one thread per block streams contiguous tiles of both vectors into
-//          a shared-memory ring with cp.async.bulk (no multicast) and an
+//          a shared-memory ring with plain cp.async.bulk copies (each block
+//          reads only this GPU's memory into its own shared memory) and an
 //          mbarrier per stage; threads decode their units from shared memory.
 #include "dot_device.cuh"
 #include "internal.hpp"

@@ -281,6 +281,7 @@ def main():
     import torch
     import torch.distributed as dist
     from accessor_universal_test_b200 import _lib, vectors
+    from accessor_universal_test_b200.sharded import allreduce_partials
 
     torch.cuda.set_device(local)
     if world > 1:
@@ -314,7 +315,7 @@ def main():
             ws.dot(fid, layout, accum, x.data_ptr(), y.data_ptr(), n, res_ptr + 8 * k, stream,
                    strategy)
         if world > 1:
-            dist.all_reduce(results)
+            allreduce_partials(results)
 
     for _ in range(args.warmup):
         step()
@@ -382,7 +383,7 @@ def main():
             ws.dot(fid, layout, accum, x.data_ptr(), y.data_ptr(), n, res_ptr + 8 * k, stream,
                    strategy)
         if world > 1:
-            dist.all_reduce(results)
+            allreduce_partials(results)
         host_out.copy_(results, non_blocking=True)
 
     for _ in range(3):
