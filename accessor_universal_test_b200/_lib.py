@@ -24,6 +24,8 @@ DENSE, PADDED = 0, 1
 ACC_FP32, ACC_FP64 = 0, 1
 TARGET_FP32, TARGET_FP64 = 0, 1
 STRATEGY_AUTO, STRATEGY_LDG, STRATEGY_TMA, STRATEGY_SCALAR = 0, 1, 2, 3
+(DECODER_AUTO, DECODER_DIRECT, DECODER_FULL_LUT, DECODER_FRACTION_LUT,
+ DECODER_FRACTION_LUT_FUSED) = range(5)
 STATUS_WAIT_TIMEOUT = 1
 GEN_SIGNED_UNIT_F64, GEN_SIGNED_UNIT_F32, GEN_NORMAL, GEN_LNS_CANCEL, GEN_POSITIVE_UNIT_F64 = range(5)
 
@@ -49,6 +51,7 @@ SIGNATURES = {
     "aut_workspace_status": (_i32, [_vp, C.POINTER(_u32), _i32]),
     "aut_dot": (_i32, [_vp, _i32, _i32, _i32, _vp, _vp, _u64, _vp, _vp]),
     "aut_dot_strategy": (_i32, [_vp, _i32, _i32, _i32, _i32, _vp, _vp, _u64, _vp, _vp]),
+    "aut_dot_variant": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _u64, _vp, _vp]),
     "aut_dot_batched": (_i32, [_vp, _i32, _i32, _i32, _vp, _vp, _u64, _u32, _u64, _vp, _vp]),
     "aut_dot_noalloc": (_i32, [_i32, _i32, _i32, _vp, _vp, _u64, _u32, _u64, _vp, _vp]),
     "aut_decode": (_i32, [_vp, _i32, _i32, _i32, _vp, _u64, _vp, _vp]),
@@ -137,9 +140,9 @@ class Workspace:
         check(load().aut_workspace_prepare(self.handle, fmt))
 
     def dot(self, fmt, layout, accum, x_ptr, y_ptr, n, result_ptr, stream=0,
-            strategy: int = 0) -> None:
-        check(load().aut_dot_strategy(self.handle, fmt, layout, accum, strategy, x_ptr,
-                                      y_ptr, n, result_ptr, stream))
+            strategy: int = 0, decoder: int = 0) -> None:
+        check(load().aut_dot_variant(self.handle, fmt, layout, accum, strategy, decoder,
+                                     x_ptr, y_ptr, n, result_ptr, stream))
 
     def status(self, clear: bool = True) -> int:
         word = C.c_uint32()

@@ -202,20 +202,29 @@ template <typename T> struct lns8_codec {
     for (int e = threadIdx.x; e < 256 * 32; e += kThreads) s[e] = g[e >> 5];
   }
 
+  // Byte k of a word is moved to bits [0, 8) by one byte permute (ALU pipe)
+  // and scaled into a table offset by one integer multiply-add (FMA pipe),
+  // so the two decode steps of every code use different pipes.
   template <int NV, class Acc>
   __device__ __forceinline__ static void values(const uint32_t *xw,
                                                 const uint32_t *yw, Acc &acc,
                                                 float *,
                                                 const unsigned char *smem) {
-    const T *tab = reinterpret_cast<const T *>(smem) + (threadIdx.x & 31);
+    constexpr uint32_t kEntryBytes = 32 * sizeof(T);
+    const uint32_t lane_off = (threadIdx.x & 31) * static_cast<uint32_t>(sizeof(T));
 #pragma unroll
-    for (int v = 0; v < NV; ++v) {
-      const T a = tab[field_low<8, 8>(xw, v) << 5];
-      const T b = tab[field_low<8, 8>(yw, v) << 5];
-      if constexpr (sizeof(T) == 4)
-        acc.mac(v, a, b);
-      else
-        acc.mac_d(v, a, b);
+    for (int w = 0; w < NV / 4; ++w) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t bx = __byte_perm(xw[w], 0u, 0x4440u + k);
+        const uint32_t by = __byte_perm(yw[w], 0u, 0x4440u + k);
+        const T a = *reinterpret_cast<const T *>(smem + (bx * kEntryBytes + lane_off));
+        const T b = *reinterpret_cast<const T *>(smem + (by * kEntryBytes + lane_off));
+        if constexpr (sizeof(T) == 4)
+          acc.mac(4 * w + k, a, b);
+        else
+          acc.mac_d(4 * w + k, a, b);
+      }
     }
   }
 
@@ -292,6 +301,195 @@ template <typename T> struct lns16_codec {
     const T *tab = reinterpret_cast<const T *>(smem);
     acc.mac_d(0, static_cast<double>(decode(load_code<16, 16>(xb, i), tab)),
               static_cast<double>(decode(load_code<16, 16>(yb, i), tab)));
+  }
+};
+
+// lns16_r11, FP32, one lookup per code: the 32768 sign-free codes decode
+// through a 128 KiB shared table (entry i = host exp2f of code i, entry
+// 0x4000 = +0 for the reserved code); the product's sign is applied once per
+// pair (sign bits of both words XORed), and the negative reserved code (NaN)
+// is made NaN explicitly, since it reads the zero entry.
+struct lns16_full_codec {
+  static constexpr int kS = 16;
+  static constexpr int kU = 4;
+  static constexpr int kTableBytes = 32768 * 4;
+  static constexpr bool kExactLanes = false;
+  __device__ static void prepare(const void *table, unsigned char *smem) {
+    const uint4 *g = static_cast<const uint4 *>(table);
+    uint4 *s = reinterpret_cast<uint4 *>(smem);
+    for (int e = threadIdx.x; e < 32768 / 4; e += kThreads) s[e] = g[e];
+  }
+
+  __device__ __forceinline__ static float at(const unsigned char *smem, uint32_t off) {
+    return *reinterpret_cast<const float *>(smem + off);
+  }
+
+  template <int NV, class Acc>
+  __device__ __forceinline__ static void values(const uint32_t *xw,
+                                                const uint32_t *yw, Acc &acc,
+                                                float *,
+                                                const unsigned char *smem) {
+    static_assert(NV % 2 == 0, "two codes per word");
+#pragma unroll
+    for (int w = 0; w < NV / 2; ++w) {
+      const uint32_t x = xw[w], y = yw[w];
+      float xl = at(smem, (x << 2) & 0x1fffcu);
+      float xh = at(smem, (x >> 14) & 0x1fffcu);
+      const float yl = at(smem, (y << 2) & 0x1fffcu);
+      const float yh = at(smem, (y >> 14) & 0x1fffcu);
+      const uint32_t sgn = x ^ y;  // product signs at bits 15 and 31
+      const uint32_t nan = __vcmpeq2(x, 0xc000c000u) | __vcmpeq2(y, 0xc000c000u);
+      xl = __uint_as_float(__float_as_uint(xl) ^ ((sgn << 16) & 0x80000000u) |
+                           ((nan << 16) & 0x7fc00000u));
+      xh = __uint_as_float((__float_as_uint(xh) ^ (sgn & 0x80000000u)) |
+                           (nan & 0x7fc00000u));
+      acc.mac(2 * w, xl, yl);
+      acc.mac(2 * w + 1, xh, yh);
+    }
+  }
+
+  template <class Acc>
+  __device__ __forceinline__ static void scalar(const unsigned char *xb,
+                                                const unsigned char *yb,
+                                                uint64_t i, Acc &acc,
+                                                const unsigned char *smem) {
+    const uint32_t cx = load_code<16, 16>(xb, i), cy = load_code<16, 16>(yb, i);
+    auto dec = [&](uint32_t c) {
+      if (c == 0xc000u) return __uint_as_float(0x7fc00000u);
+      const float m = at(smem, (c & 0x7fffu) << 2);
+      return (c & 0x8000u) ? -m : m;
+    };
+    acc.mac_d(0, static_cast<double>(dec(cx)), static_cast<double>(dec(cy)));
+  }
+};
+
+// lns16_r11 with the fused multiply (lns_decoder_strategies.cuh:353-367): the
+// product of two LNS values is 2^((cx + cy) / 2048), so the two log codes are
+// added and a single fraction-table lookup serves the pair.  Each 15-bit log
+// code is biased by 2^14 (reserved code -> 0, finite codes -> [1, 2^15)), so
+// one 32-bit add sums both halfwords of a word pair without a carry crossing
+// them: halfword h = cx + cy + 2^15, whose low 11 bits index the fraction
+// table and whose top 5 bits are the binary exponent + 16.  The shared copy
+// of the table is pre-scaled by 2^-16, so the exponent is one integer add of
+// (h >> 11) into the exponent field and the product's sign one more add of
+// bit 31.  Products lie in [2^-16, 2^16): always normal, never rounded
+// again.  Reserved codes follow lns::multiply_codes
+// (lns_benchmark_core.hpp:241-254) without branches: adding 0x7fff to a
+// biased halfword sets its top bit exactly when the code is not reserved, a
+// sign-replicating byte permute spreads that bit into a mask that zeroes
+// products with a zero operand, and a reserved code with its sign bit set
+// (NaN) raises a flag that makes the DOT NaN.
+template <typename T> struct lns16_fused_codec {
+  static constexpr int kS = 16;
+  static constexpr int kU = 4;
+  static constexpr int kTableBytes = 2048 * static_cast<int>(sizeof(T));
+  static constexpr bool kExactLanes = false;
+  static constexpr int kMant = sizeof(T) == 4 ? 23 : 20;  // exponent shift in the top word
+  __device__ static void prepare(const void *table, unsigned char *smem) {
+    const T *g = static_cast<const T *>(table);
+    T *s = reinterpret_cast<T *>(smem);
+    for (int e = threadIdx.x; e < 2048; e += kThreads) {
+      if constexpr (sizeof(T) == 4) {
+        s[e] = __uint_as_float(__float_as_uint(g[e]) - (16u << kMant));
+      } else {
+        const double t = g[e];
+        s[e] = __hiloint2double(__double2hiint(t) - (16 << kMant), __double2loint(t));
+      }
+    }
+  }
+
+  // every byte = copies of bit 7 of byte k of v (prmt sign replication)
+  template <int K> __device__ __forceinline__ static uint32_t spread(uint32_t v) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(v), "r"(0u), "n"(0x8888 + 0x1111 * K));
+    return r;
+  }
+
+  // product from the biased log sum h (bits [0, 16)) and the sign bit at 31
+  __device__ __forceinline__ static T product(uint32_t h, uint32_t sign, const T *tab) {
+    const uint32_t e = (h >> 11) << kMant;
+    if constexpr (sizeof(T) == 4) {
+      return __uint_as_float(__float_as_uint(tab[h & 0x7ffu]) + e + sign);
+    } else {
+      const double t = tab[h & 0x7ffu];
+      return __hiloint2double(static_cast<int>(static_cast<uint32_t>(__double2hiint(t)) + e + sign),
+                              __double2loint(t));
+    }
+  }
+
+  // product() with all bits cleared where the mask is 0 (a zero operand)
+  __device__ __forceinline__ static T masked(T v, uint32_t mask) {
+    if constexpr (sizeof(T) == 4) {
+      return __uint_as_float(__float_as_uint(v) & mask);
+    } else {
+      return __hiloint2double(static_cast<int>(static_cast<uint32_t>(__double2hiint(v)) & mask),
+                              static_cast<int>(static_cast<uint32_t>(__double2loint(v)) & mask));
+    }
+  }
+
+  // the exact product of two codes, specials included
+  __device__ __forceinline__ static T multiply(uint32_t cx, uint32_t cy, const T *tab) {
+    const uint32_t bx = (cx & 0x7fffu) ^ 0x4000u, by = (cy & 0x7fffu) ^ 0x4000u;
+    const bool nan_x = bx == 0 && (cx & 0x8000u), nan_y = by == 0 && (cy & 0x8000u);
+    if (nan_x || nan_y) {
+      if constexpr (sizeof(T) == 4) return __uint_as_float(0x7fc00000u);
+      else return __hiloint2double(0x7ff80000, 0);
+    }
+    const uint32_t sign = ((cx ^ cy) & 0x8000u) << 16;
+    if (bx == 0 || by == 0) {
+      if constexpr (sizeof(T) == 4) return __uint_as_float(sign);
+      else return __hiloint2double(static_cast<int>(sign), 0);
+    }
+    return product(bx + by, sign, tab);
+  }
+
+  template <class Acc>
+  __device__ __forceinline__ static void add(Acc &acc, int slot, T p) {
+    if constexpr (sizeof(T) == 4)
+      acc.mac(slot, p, 1.0f);
+    else
+      acc.mac_d(slot, p, 1.0);
+  }
+
+  template <int NV, class Acc>
+  __device__ __forceinline__ static void values(const uint32_t *xw,
+                                                const uint32_t *yw, Acc &acc,
+                                                float *,
+                                                const unsigned char *smem) {
+    static_assert(NV % 2 == 0, "two codes per word");
+    const T *tab = reinterpret_cast<const T *>(smem);
+    uint32_t nan = 0;
+#pragma unroll
+    for (int w = 0; w < NV / 2; ++w) {
+      const uint32_t x = xw[w], y = yw[w];
+      const uint32_t bx = (x & 0x7fff7fffu) ^ 0x40004000u;
+      const uint32_t by = (y & 0x7fff7fffu) ^ 0x40004000u;
+      const uint32_t h = bx + by;
+      // bits 15 / 31: that code is not reserved
+      const uint32_t lx = bx + 0x7fff7fffu, ly = by + 0x7fff7fffu;
+      nan |= (x & ~lx) | (y & ~ly);  // reserved with the sign bit set
+      const uint32_t live = lx & ly;
+      const uint32_t sg = x ^ y;
+      add(acc, 2 * w, masked(product(h & 0xffffu, (sg << 16) & 0x80000000u, tab), spread<1>(live)));
+      add(acc, 2 * w + 1, masked(product(h >> 16, sg & 0x80000000u, tab), spread<3>(live)));
+    }
+    if (nan & 0x80008000u) {
+      if constexpr (sizeof(T) == 4)
+        add(acc, 0, __uint_as_float(0x7fc00000u));
+      else
+        add(acc, 0, __hiloint2double(0x7ff80000, 0));
+    }
+  }
+
+  template <class Acc>
+  __device__ __forceinline__ static void scalar(const unsigned char *xb,
+                                                const unsigned char *yb,
+                                                uint64_t i, Acc &acc,
+                                                const unsigned char *smem) {
+    const T *tab = reinterpret_cast<const T *>(smem);
+    acc.mac_d(0, static_cast<double>(multiply(load_code<16, 16>(xb, i),
+                                              load_code<16, 16>(yb, i), tab)),
+              1.0);
   }
 };
 
@@ -380,6 +578,13 @@ template <int S> struct tma_shape {
   static constexpr int UV = S == 64 ? 1 : 32 / G;  // codes per unit
   static constexpr int VPT = S >= 24 ? 16 : 32;    // codes per thread per tile
   static constexpr int V = VPT / UV;               // units per thread per tile
+  // Units of one or two words are read four words at a time: one 16-byte
+  // shared load per operand, a quarter warp covering 128 contiguous bytes
+  // (no bank conflicts), and one decode call per four words.  Longer units
+  // have an odd word count and are read word by word, one unit per lane,
+  // which is conflict-free too.
+  static constexpr int GROUP = UW <= 2 ? 4 / UW : 1;  // units per load
+  static constexpr int LW = UW * GROUP;              // words per load
   static constexpr int TILE_WORDS = kThreads * V * UW;
   static constexpr int TILE_BYTES = TILE_WORDS * 4;  // per vector
   static constexpr uint64_t TILE_VALUES = static_cast<uint64_t>(kThreads) * VPT;
@@ -388,6 +593,7 @@ template <int S> struct tma_shape {
   static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
   static_assert(TILE_BYTES % 16 == 0, "bulk copies move 16-byte multiples");
   static_assert(V * UV == VPT, "units tile the thread's codes");
+  static_assert(V % GROUP == 0, "loads tile the thread's units");
 };
 
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 2 GHz
@@ -446,9 +652,10 @@ __global__ void __launch_bounds__(kThreads)
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ double scratch[kThreads / 32];
   using shape = tma_shape<Codec::kS>;
-  constexpr int UW = shape::UW;
   constexpr int UV = shape::UV;
   constexpr int V = shape::V;
+  constexpr int GROUP = shape::GROUP;
+  constexpr int LW = shape::LW;
   constexpr int STAGES = shape::STAGES;
   constexpr int TILE_BYTES = shape::TILE_BYTES;
   __shared__ __align__(8) uint64_t full[STAGES];
@@ -490,15 +697,22 @@ __global__ void __launch_bounds__(kThreads)
         reinterpret_cast<const uint32_t *>(ring + (k % STAGES) * (2 * TILE_BYTES));
     const uint32_t *ys = xs + shape::TILE_WORDS;
 #pragma unroll
-    for (int v = 0; v < V; ++v) {
-      const int u = threadIdx.x + v * kThreads;
-      uint32_t xw[UW], yw[UW];
+    for (int v = 0; v < V / GROUP; ++v) {
+      const int u = threadIdx.x + v * kThreads;  // load index
+      uint32_t xw[LW], yw[LW];
+      if constexpr (LW == 4) {
+        const uint4 a = reinterpret_cast<const uint4 *>(xs)[u];
+        const uint4 b = reinterpret_cast<const uint4 *>(ys)[u];
+        xw[0] = a.x; xw[1] = a.y; xw[2] = a.z; xw[3] = a.w;
+        yw[0] = b.x; yw[1] = b.y; yw[2] = b.z; yw[3] = b.w;
+      } else {
 #pragma unroll
-      for (int w = 0; w < UW; ++w) {
-        xw[w] = xs[u * UW + w];
-        yw[w] = ys[u * UW + w];
+        for (int w = 0; w < LW; ++w) {
+          xw[w] = xs[u * LW + w];
+          yw[w] = ys[u * LW + w];
+        }
       }
-      Codec::template values<UV>(xw, yw, acc, lanes, smem);
+      Codec::template values<UV * GROUP>(xw, yw, acc, lanes, smem);
     }
     flush_tile<Codec>(acc, lanes);
     // Every thread is done with this stage (and the exit decision is the
@@ -574,32 +788,62 @@ kernel_entry pick(int strategy, int accum, int table_kind) {
              : make_entry<Codec, aut::dev::acc_f64>(strategy, table_kind);
 }
 
-// The strategy AUTO resolves to per format, chosen from CUDA-event timings
-// of both strategies at N = 2^27 on B200 (packed GB/s, FP32 accumulator):
-//   fp32 6916 LDG / 6636 TMA     fp64  7106 / 7242     e2m3 5140 / 4642
+// The strategy AUTO resolves to per format and accumulator, chosen from
+// CUDA-event timings of both strategies at N = 2^27 on B200 (packed GB/s,
+// LDG / TMA, FP32 accumulator):
+//   fp32 6916 / 6636     fp64  7106 / 7242     e2m3 5140 / 4642
 //   e8m0 4294 / 5529     e8m1 5517 / 5846     e8m3 5841 / 6090
 //   e8m5 4543 / 6377     bf16 6636 / 6519     e8m15 6417 / 6689
-//   lns8_r3 3580 / 3395  lns16_r11 3540 / 3648
+//   lns8_r3 4835 / 5116 (FP64 accumulator: 3677 / 2444)
+//   lns16_r11 (fused multiply) 4686 / 4589 (FP64: 3710 / 3631)
 // Packets of several 16-byte vectors (S = 9, 10, 12, 14, 24) load strided
 // per thread and stall on the LSU queue; the bulk-copy ring removes that.
-// Decode-bound formats (e2m3, lns8) lose more to the staging instructions
-// than they gain.
-int auto_strategy(int32_t format, int32_t layout) {
+// e2m3 loses more to the staging instructions than it gains; lns8 with FP64
+// has a 64 KiB table, and beside the 64 KiB ring only one block fits an SM.
+int auto_strategy(int32_t format, int32_t layout, int32_t accum) {
   (void)layout;
   switch (format) {
   case AUT_FMT_FP32:
   case AUT_FMT_E2M3:
   case AUT_FMT_BF16_E8M7:
-  case AUT_FMT_LNS8_R3: return AUT_STRATEGY_LDG;
+  case AUT_FMT_LNS16_R11: return AUT_STRATEGY_LDG;
+  case AUT_FMT_LNS8_R3:
+    return accum == AUT_ACCUM_FP32 ? AUT_STRATEGY_TMA : AUT_STRATEGY_LDG;
   default: return AUT_STRATEGY_TMA;
   }
 }
 
-kernel_entry lookup(int32_t format, int32_t layout, int32_t accum, int strategy) {
+// Decoders per format (the reference's decoder_kind axis): the E8 formats,
+// raw storage and e2m3 decode DIRECT (bit moves / hardware conversion);
+// lns8_r3 has FULL_LUT; lns16_r11 has FULL_LUT (FP32 only: the table is
+// 128 KiB of FP32), FRACTION_LUT and FRACTION_LUT_FUSED.  AUTO picks the
+// fastest measured one.
+kernel_entry lookup(int32_t format, int32_t layout, int32_t accum, int strategy,
+                    int decoder = AUT_DECODER_AUTO) {
   using namespace aut::dev;
-  if (strategy == AUT_STRATEGY_AUTO) strategy = auto_strategy(format, layout);
+  if (strategy == AUT_STRATEGY_AUTO) strategy = auto_strategy(format, layout, accum);
   const bool dense = layout == AUT_LAYOUT_DENSE;
   const int s = strategy;
+  const bool lns = format == AUT_FMT_LNS8_R3 || format == AUT_FMT_LNS16_R11;
+  if (decoder != AUT_DECODER_AUTO) {
+    if (!lns && decoder != AUT_DECODER_DIRECT) return {};
+    if (lns && decoder == AUT_DECODER_DIRECT) return {};
+    if (format == AUT_FMT_LNS8_R3 && decoder != AUT_DECODER_FULL_LUT) return {};
+  }
+  if (format == AUT_FMT_LNS16_R11) {
+    const bool f32 = accum == AUT_ACCUM_FP32;
+    switch (decoder) {
+    case AUT_DECODER_FULL_LUT:
+      if (!f32) return {};
+      return make_entry<lns16_full_codec, acc_f32>(s, 1);
+    case AUT_DECODER_FRACTION_LUT:
+      return f32 ? make_entry<lns16_codec<float>, acc_f32>(s, 3)
+                 : make_entry<lns16_codec<double>, acc_f64>(s, 4);
+    default:  // AUTO, FRACTION_LUT_FUSED
+      return f32 ? make_entry<lns16_fused_codec<float>, acc_f32>(s, 3)
+                 : make_entry<lns16_fused_codec<double>, acc_f64>(s, 4);
+    }
+  }
   switch (format) {
   case AUT_FMT_FP32: return pick<e8_codec<32, 32>>(s, accum, 0);
   case AUT_FMT_FP64:
@@ -621,9 +865,6 @@ kernel_entry lookup(int32_t format, int32_t layout, int32_t accum, int strategy)
   case AUT_FMT_LNS8_R3:
     return accum == AUT_ACCUM_FP32 ? make_entry<lns8_codec<float>, acc_f32>(s, 1)
                                    : make_entry<lns8_codec<double>, acc_f64>(s, 2);
-  case AUT_FMT_LNS16_R11:
-    return accum == AUT_ACCUM_FP32 ? make_entry<lns16_codec<float>, acc_f32>(s, 3)
-                                   : make_entry<lns16_codec<double>, acc_f64>(s, 4);
   default: return {};
   }
 }
@@ -676,8 +917,8 @@ int32_t dot_supported(int32_t format, int32_t layout, int32_t accum) {
 }
 
 aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
-                      int32_t accum, int32_t strategy, const void *x,
-                      const void *y, uint64_t n, uint32_t batch,
+                      int32_t accum, int32_t strategy, int32_t decoder,
+                      const void *x, const void *y, uint64_t n, uint32_t batch,
                       uint64_t batch_stride, double *results, void *stream,
                       double *partials, unsigned int *tickets,
                       unsigned int *status, int max_blocks_total) {
@@ -685,10 +926,10 @@ aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
   // code goes through the per-value load and decode.
   const bool scalar_only = strategy == AUT_STRATEGY_SCALAR;
   kernel_entry e = lookup(format, layout, accum,
-                          scalar_only ? AUT_STRATEGY_LDG : strategy);
+                          scalar_only ? AUT_STRATEGY_LDG : strategy, decoder);
   if (e.fn == nullptr)
     return fail(AUT_ERR_UNSUPPORTED,
-                "no fused DOT kernel for this format/layout/accumulator");
+                "no fused DOT kernel for this format/layout/accumulator/decoder");
   aut_status st = blocks_per_sm(e);
   if (st != AUT_OK) return st;
 

@@ -14,8 +14,8 @@
 namespace aut::lib {
 
 aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
-                      int32_t accum, int32_t strategy, const void *x,
-                      const void *y, uint64_t n, uint32_t batch,
+                      int32_t accum, int32_t strategy, int32_t decoder,
+                      const void *x, const void *y, uint64_t n, uint32_t batch,
                       uint64_t batch_stride, double *results, void *stream,
                       double *partials, unsigned int *tickets,
                       unsigned int *status, int max_blocks_total);
@@ -532,15 +532,25 @@ aut_status aut_dot_strategy(aut_workspace *ws, int32_t format, int32_t layout,
                             int32_t accum, int32_t strategy, const void *x,
                             const void *y, uint64_t n, double *result,
                             void *stream) {
+  return aut_dot_variant(ws, format, layout, accum, strategy, AUT_DECODER_AUTO,
+                         x, y, n, result, stream);
+}
+
+aut_status aut_dot_variant(aut_workspace *ws, int32_t format, int32_t layout,
+                           int32_t accum, int32_t strategy, int32_t decoder,
+                           const void *x, const void *y, uint64_t n,
+                           double *result, void *stream) {
   clear_error();
   aut_status st = check_dot_args(ws, format, layout, accum, x, y, n, result);
   if (st != AUT_OK) return st;
   if (strategy < AUT_STRATEGY_AUTO || strategy > AUT_STRATEGY_SCALAR)
     return fail(AUT_ERR_INVALID_ARGUMENT, "unknown access strategy");
+  if (decoder < AUT_DECODER_AUTO || decoder > AUT_DECODER_FRACTION_LUT_FUSED)
+    return fail(AUT_ERR_INVALID_ARGUMENT, "unknown decoder");
   device_scope scope(ws->device);
   AUT_CUDA_TRY(scope.err);
-  return dot_launch(ws, format, layout, accum, strategy, x, y, n, 1, 0, result,
-                    stream, ws->partials, ws->tickets,
+  return dot_launch(ws, format, layout, accum, strategy, decoder, x, y, n, 1, 0,
+                    result, stream, ws->partials, ws->tickets,
                     ws->tickets + kMaxBatchPerLaunch, ws->max_blocks);
 }
 
@@ -557,8 +567,9 @@ aut_status aut_dot_batched(aut_workspace *ws, int32_t format, int32_t layout,
     return fail(AUT_ERR_INVALID_ARGUMENT, "batch stride smaller than one vector");
   device_scope scope(ws->device);
   AUT_CUDA_TRY(scope.err);
-  return dot_launch(ws, format, layout, accum, AUT_STRATEGY_AUTO, x, y, n,
-                    batch, batch_stride_bytes, results, stream, ws->partials,
+  return dot_launch(ws, format, layout, accum, AUT_STRATEGY_AUTO,
+                    AUT_DECODER_AUTO, x, y, n, batch, batch_stride_bytes,
+                    results, stream, ws->partials,
                     ws->tickets, ws->tickets + kMaxBatchPerLaunch,
                     ws->max_blocks);
 }

@@ -343,23 +343,33 @@ def main():
     # strategy in use and for each explicit access strategy
     reps = 20
 
-    def time_kernel(k, strat):
+    def time_kernel(k, strat, dec=0):
         x, y = inputs[k]
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for _ in range(reps):
             ws.dot(fids[k], layout, accum, x.data_ptr(), y.data_ptr(), n, res_ptr + 8 * k,
-                   stream, strat)
+                   stream, strat, dec)
         b.record()
         torch.cuda.synchronize()
         return a.elapsed_time(b) / reps
 
-    per_kernel, by_strategy = [], {}
+    per_kernel, by_strategy, by_decoder = [], {}, {}
     for k, fid in enumerate(fids):
         t_ms = time_kernel(k, strategy)
         per_kernel.append((fmts[k][0], t_ms, packed_bytes[k] / (t_ms / 1e3) / 1e9))
         by_strategy[fmts[k][0]] = {name: packed_bytes[k] / (time_kernel(k, s) / 1e3) / 1e9
                                    for name, s in (("ldg", 1), ("tma", 2))}
+        # every decoder this format/accumulator has, each with both strategies
+        table = {}
+        for dname, dec in (("direct", 1), ("full_lut", 2), ("fraction_lut", 3),
+                           ("fraction_lut_fused", 4)):
+            for sname, s in (("ldg", 1), ("tma", 2)):
+                try:
+                    table[f"{dname}/{sname}"] = packed_bytes[k] / (time_kernel(k, s, dec) / 1e3) / 1e9
+                except _lib.AutError:
+                    pass
+        by_decoder[fmts[k][0]] = table
     if ws.status() != 0:
         raise RuntimeError("a bounded device wait timed out during the benchmark")
     peak, peak_kind = measured_peak()
@@ -440,7 +450,8 @@ def main():
         "decoded_elems_per_s": elems,
         "pct_of_8tbs": value / world / 8000.0 * 100.0,
         "per_format": [{"format": f, "ms": t, "gbs": g, "frac_of_peak": g / peak,
-                        "gbs_by_strategy": by_strategy[f]}
+                        "gbs_by_strategy": by_strategy[f],
+                        "gbs_by_decoder": by_decoder[f]}
                        for f, t, g in per_kernel],
         "strategy": args.strategy,
         "normalized_error": errors or None,

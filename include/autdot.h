@@ -86,6 +86,18 @@ enum {
                              access method); the slow baseline            */
 };
 
+/* How the fused DOT turns codes into values (decoder_kind,
+ * bitwidth_benchmark_core.hpp:25-40, lns_decoder_strategies.cuh:19-34).
+ * AUTO picks the measured best per format and accumulator. */
+enum {
+  AUT_DECODER_AUTO = 0,
+  AUT_DECODER_DIRECT = 1,      /* bit moves / hardware conversion (E8, e2m3, raw) */
+  AUT_DECODER_FULL_LUT = 2,     /* one shared-memory lookup per code (LNS)     */
+  AUT_DECODER_FRACTION_LUT = 3, /* fraction table + exponent add (lns16_r11)   */
+  AUT_DECODER_FRACTION_LUT_FUSED = 4 /* logs added, one fraction lookup per
+                                        pair: multiply_kind::fused (lns16_r11) */
+};
+
 /* Sticky device status bits reported by aut_workspace_status(). */
 enum {
   AUT_STATUS_WAIT_TIMEOUT = 1 /* a bounded pipeline wait gave up; the
@@ -162,6 +174,15 @@ aut_status aut_dot_strategy(aut_workspace *ws, int32_t format, int32_t layout,
                             int32_t accum, int32_t strategy, const void *x,
                             const void *y, uint64_t n, double *result,
                             void *stream);
+
+/* aut_dot with explicit access strategy and decoder (AUT_DECODER_*), the two
+ * axes of the reference's strategy matrix (src/bitwidth_strategy_bench.cu:744-782,
+ * src/lns_strategy_bench.cu:961-1025).  Combinations without a kernel return
+ * AUT_ERR_UNSUPPORTED. */
+aut_status aut_dot_variant(aut_workspace *ws, int32_t format, int32_t layout,
+                           int32_t accum, int32_t strategy, int32_t decoder,
+                           const void *x, const void *y, uint64_t n,
+                           double *result, void *stream);
 
 /* `batch` independent DOTs in one launch: pair b reads
  * x + b*batch_stride_bytes and y + b*batch_stride_bytes; results[b]. */

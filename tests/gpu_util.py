@@ -33,12 +33,12 @@ def device_pair(ws, name, layout, n, seed=SEED):
 STRATEGIES = [1, 2, 3]  # LDG (registers), TMA (bulk copies into shared memory), SCALAR
 
 
-def gpu_dot(ws, name, layout, accum, x, y, n, x_off=0, y_off=0, strategy=0):
+def gpu_dot(ws, name, layout, accum, x, y, n, x_off=0, y_off=0, strategy=0, decoder=0):
     import torch
     from accessor_universal_test_b200 import _lib
     res = torch.full((1,), float("nan"), dtype=torch.float64, device=x.device)
     ws.dot(_lib.format_id(name), layout, accum, x.data_ptr() + x_off,
-           y.data_ptr() + y_off, n, res.data_ptr(), strategy=strategy)
+           y.data_ptr() + y_off, n, res.data_ptr(), strategy=strategy, decoder=decoder)
     torch.cuda.synchronize()
     assert ws.status() == 0, "a bounded device wait timed out"
     return float(res.item())

@@ -35,6 +35,43 @@ def test_dot_matches_oracle(ws, orc, name, layout, strategy):
                 assert got == float(ref_dot), (name, n, got, float(ref_dot))
 
 
+# (format, accumulator, decoder) triples with a kernel; every other explicit
+# decoder is AUT_ERR_UNSUPPORTED.
+DECODER_CASES = [("lns8_r3", 0, 2), ("lns8_r3", 1, 2), ("lns16_r11", 0, 2),
+                 ("lns16_r11", 0, 3), ("lns16_r11", 1, 3), ("lns16_r11", 0, 4),
+                 ("lns16_r11", 1, 4), ("e8m5", 0, 1), ("e2m3", 1, 1), ("fp32", 0, 1)]
+
+
+@pytest.mark.parametrize("name,accum,decoder", DECODER_CASES)
+@pytest.mark.parametrize("strategy", STRATEGIES)
+def test_every_decoder_matches_oracle(ws, orc, name, accum, decoder, strategy):
+    for n in (3, 4099, (1 << 20) + 37):
+        x, y = device_pair(ws, name, 0, n)
+        ref_dot, ref_abs = oracle_dot(orc, name, n)
+        got = gpu_dot(ws, name, 0, accum, x, y, n, strategy=strategy, decoder=decoder)
+        err = normalized_error(got, ref_dot, ref_abs)
+        assert err <= TOL[accum], (name, accum, decoder, n, got, float(ref_dot), float(err))
+
+
+def test_decoders_without_a_kernel_are_refused(ws):
+    import torch
+    from accessor_universal_test_b200 import _lib
+    x = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+    res = torch.zeros(1, dtype=torch.float64, device="cuda")
+    refused = [("lns16_r11", 1, 2), ("lns16_r11", 0, 1), ("lns8_r3", 0, 3),
+               ("lns8_r3", 0, 4), ("lns8_r3", 0, 1), ("e8m0", 0, 2), ("fp32", 0, 3),
+               ("e8m15", 1, 4)]
+    for name, accum, decoder in refused:
+        with pytest.raises(_lib.AutError) as info:
+            ws.dot(_lib.format_id(name), 0, accum, x.data_ptr(), x.data_ptr(), 64,
+                   res.data_ptr(), decoder=decoder)
+        assert info.value.status == _lib.AUT_ERR_UNSUPPORTED, (name, accum, decoder)
+    with pytest.raises(_lib.AutError) as info:
+        ws.dot(_lib.format_id("e8m0"), 0, 0, x.data_ptr(), x.data_ptr(), 64,
+               res.data_ptr(), decoder=5)
+    assert info.value.status == _lib.AUT_ERR_INVALID_ARGUMENT
+
+
 def _fnv_words(words):
     h = 1469598103934665603
     for w in words.astype(np.uint64).tolist():
@@ -136,6 +173,54 @@ def test_special_codes_propagate_like_the_oracle(ws, orc, name):
                     assert got == want, (name, label, pos, got, want)
                 else:
                     assert abs(got - want) <= TOL[accum] * s[0], (name, label, pos, got, want)
+
+
+LNS_DECODERS = [("lns8_r3", 0, 2), ("lns8_r3", 1, 2), ("lns16_r11", 0, 2),
+                ("lns16_r11", 0, 3), ("lns16_r11", 1, 3), ("lns16_r11", 0, 4),
+                ("lns16_r11", 1, 4)]
+
+
+@pytest.mark.parametrize("name,accum,decoder", LNS_DECODERS)
+@pytest.mark.parametrize("strategy", STRATEGIES)
+def test_lns_reserved_codes_in_every_decoder(ws, orc, name, accum, decoder, strategy):
+    """Zero and NaN codes (the reserved log code with either sign), sparse
+    and dense, in one or both operands: zero products vanish and any NaN
+    operand makes the DOT NaN (lns::multiply_codes)."""
+    import torch
+    from accessor_universal_test_b200 import _lib
+    fid = _lib.format_id(name)
+    desc = _lib.format_info(fid)
+    n = 70_001
+    _, _, cx = oracle_codes(orc, name, n, 0)
+    _, _, cy = oracle_codes(orc, name, n, 1)
+    zero = orc.encode(desc, [0.0])[0]
+    nan = orc.encode(desc, [np.nan])[0]
+    rng = np.random.default_rng(7)
+    cases = {
+        "sparse zeros in x": (rng.random(n) < 0.001, None, zero),
+        "dense zeros in x and y": (rng.random(n) < 0.3, rng.random(n) < 0.3, zero),
+        "one nan in y": (None, np.arange(n) == 40_000, nan),
+    }
+    for label, (mx, my, code) in cases.items():
+        xx, yy = cx.copy(), cy.copy()
+        if mx is not None:
+            xx[mx] = code
+        if my is not None:
+            yy[my] = code
+        with np.errstate(invalid="ignore"):
+            plain = (orc.decode_f64(desc, xx) * orc.decode_f64(desc, yy)).sum()
+        (d, s) = orc.dot_codes(desc, xx, yy, threads=4)
+        bufs = []
+        for codes in (xx, yy):
+            b = np.zeros(_lib.storage_bytes(fid, 0, n), np.uint8)
+            _lib.check(_lib.load().aut_pack_host(fid, 0, codes.ctypes.data, n, b.ctypes.data))
+            bufs.append(torch.from_numpy(b).cuda())
+        got = gpu_dot(ws, name, 0, accum, bufs[0], bufs[1], n, strategy=strategy,
+                      decoder=decoder)
+        if np.isnan(plain):
+            assert np.isnan(got), label
+        else:
+            assert abs(got - d[0]) <= TOL[accum] * s[0], (label, got, d[0])
 
 
 @pytest.mark.parametrize("name", ["e8m0", "e2m3", "lns16_r11", "fp32"])
