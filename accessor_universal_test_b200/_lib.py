@@ -53,6 +53,7 @@ SIGNATURES = {
     "aut_dot_strategy": (_i32, [_vp, _i32, _i32, _i32, _i32, _vp, _vp, _u64, _vp, _vp]),
     "aut_dot_variant": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _u64, _vp, _vp]),
     "aut_dot_batched": (_i32, [_vp, _i32, _i32, _i32, _vp, _vp, _u64, _u32, _u64, _vp, _vp]),
+    "aut_gemv": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _u64, _u64, _vp, _vp]),
     "aut_dot_noalloc": (_i32, [_i32, _i32, _i32, _vp, _vp, _u64, _u32, _u64, _vp, _vp]),
     "aut_decode": (_i32, [_vp, _i32, _i32, _i32, _vp, _u64, _vp, _vp]),
     "aut_encode": (_i32, [_vp, _i32, _i32, _vp, _u64, _vp, _vp]),
@@ -153,6 +154,11 @@ class Workspace:
                     results_ptr, stream=0) -> None:
         check(load().aut_dot_batched(self.handle, fmt, layout, accum, x_ptr, y_ptr, n,
                                      batch, stride_bytes, results_ptr, stream))
+
+    def gemv(self, fmt, layout, accum, matrix_ptr, vector_ptr, rows, columns, result_ptr,
+             stream=0, strategy: int = 0, decoder: int = 0) -> None:
+        check(load().aut_gemv(self.handle, fmt, layout, accum, strategy, decoder, matrix_ptr,
+                              vector_ptr, rows, columns, result_ptr, stream))
 
     def decode(self, fmt, layout, target, codes_ptr, n, out_ptr, stream=0) -> None:
         check(load().aut_decode(self.handle, fmt, layout, target, codes_ptr, n, out_ptr, stream))

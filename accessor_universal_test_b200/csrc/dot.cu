@@ -30,7 +30,12 @@ struct dot_params {
   const unsigned char *x;
   const unsigned char *y;
   uint64_t n;
-  uint64_t batch_stride;  // bytes between the pairs of a batch
+  uint64_t x_stride;      // bytes between the pairs of a batch
+  uint64_t y_stride;
+  uint64_t x_first;       // value index of this launch's first x / y (per-value path)
+  uint64_t y_first;
+  uint64_t x_index_stride;  // values between pairs whose streams do not start
+  uint64_t y_index_stride;  // on a byte (per-value path only)
   int vector_ok;          // both streams 16-byte aligned
   const void *table;      // decode table (LNS formats)
   double *partials;       // [gridDim.y][gridDim.x]
@@ -70,12 +75,12 @@ template <int S, int W> struct e8_codec {
   }
 
   template <class Acc>
-  __device__ __forceinline__ static void scalar(const unsigned char *xb,
-                                                const unsigned char *yb,
-                                                uint64_t i, Acc &acc,
+  __device__ __forceinline__ static void scalar(const unsigned char *xb, uint64_t i,
+                                                const unsigned char *yb, uint64_t j,
+                                                Acc &acc,
                                                 const unsigned char *) {
     const float a = __uint_as_float(load_code<S, W>(xb, i) << (32 - W));
-    const float b = __uint_as_float(load_code<S, W>(yb, i) << (32 - W));
+    const float b = __uint_as_float(load_code<S, W>(yb, j) << (32 - W));
     acc.mac_d(0, static_cast<double>(a), static_cast<double>(b));
   }
 };
@@ -103,12 +108,12 @@ struct f64_codec {
   }
 
   template <class Acc>
-  __device__ __forceinline__ static void scalar(const unsigned char *xb,
-                                                const unsigned char *yb,
-                                                uint64_t i, Acc &acc,
+  __device__ __forceinline__ static void scalar(const unsigned char *xb, uint64_t i,
+                                                const unsigned char *yb, uint64_t j,
+                                                Acc &acc,
                                                 const unsigned char *) {
     acc.mac_d(0, __ldg(reinterpret_cast<const double *>(xb) + i),
-              __ldg(reinterpret_cast<const double *>(yb) + i));
+              __ldg(reinterpret_cast<const double *>(yb) + j));
   }
 };
 
@@ -178,12 +183,12 @@ template <int S> struct e2m3_codec {
   }
 
   template <class Acc>
-  __device__ __forceinline__ static void scalar(const unsigned char *xb,
-                                                const unsigned char *yb,
-                                                uint64_t i, Acc &acc,
+  __device__ __forceinline__ static void scalar(const unsigned char *xb, uint64_t i,
+                                                const unsigned char *yb, uint64_t j,
+                                                Acc &acc,
                                                 const unsigned char *) {
     acc.mac_d(0, static_cast<double>(decode1(load_code<S, 6>(xb, i))),
-              static_cast<double>(decode1(load_code<S, 6>(yb, i))));
+              static_cast<double>(decode1(load_code<S, 6>(yb, j))));
   }
 };
 
@@ -229,13 +234,13 @@ template <typename T> struct lns8_codec {
   }
 
   template <class Acc>
-  __device__ __forceinline__ static void scalar(const unsigned char *xb,
-                                                const unsigned char *yb,
-                                                uint64_t i, Acc &acc,
+  __device__ __forceinline__ static void scalar(const unsigned char *xb, uint64_t i,
+                                                const unsigned char *yb, uint64_t j,
+                                                Acc &acc,
                                                 const unsigned char *smem) {
     const T *tab = reinterpret_cast<const T *>(smem) + (threadIdx.x & 31);
     acc.mac_d(0, static_cast<double>(tab[load_code<8, 8>(xb, i) << 5]),
-              static_cast<double>(tab[load_code<8, 8>(yb, i) << 5]));
+              static_cast<double>(tab[load_code<8, 8>(yb, j) << 5]));
   }
 };
 
@@ -294,13 +299,13 @@ template <typename T> struct lns16_codec {
   }
 
   template <class Acc>
-  __device__ __forceinline__ static void scalar(const unsigned char *xb,
-                                                const unsigned char *yb,
-                                                uint64_t i, Acc &acc,
+  __device__ __forceinline__ static void scalar(const unsigned char *xb, uint64_t i,
+                                                const unsigned char *yb, uint64_t j,
+                                                Acc &acc,
                                                 const unsigned char *smem) {
     const T *tab = reinterpret_cast<const T *>(smem);
     acc.mac_d(0, static_cast<double>(decode(load_code<16, 16>(xb, i), tab)),
-              static_cast<double>(decode(load_code<16, 16>(yb, i), tab)));
+              static_cast<double>(decode(load_code<16, 16>(yb, j), tab)));
   }
 };
 
@@ -349,11 +354,11 @@ struct lns16_full_codec {
   }
 
   template <class Acc>
-  __device__ __forceinline__ static void scalar(const unsigned char *xb,
-                                                const unsigned char *yb,
-                                                uint64_t i, Acc &acc,
+  __device__ __forceinline__ static void scalar(const unsigned char *xb, uint64_t i,
+                                                const unsigned char *yb, uint64_t j,
+                                                Acc &acc,
                                                 const unsigned char *smem) {
-    const uint32_t cx = load_code<16, 16>(xb, i), cy = load_code<16, 16>(yb, i);
+    const uint32_t cx = load_code<16, 16>(xb, i), cy = load_code<16, 16>(yb, j);
     auto dec = [&](uint32_t c) {
       if (c == 0xc000u) return __uint_as_float(0x7fc00000u);
       const float m = at(smem, (c & 0x7fffu) << 2);
@@ -482,13 +487,13 @@ template <typename T> struct lns16_fused_codec {
   }
 
   template <class Acc>
-  __device__ __forceinline__ static void scalar(const unsigned char *xb,
-                                                const unsigned char *yb,
-                                                uint64_t i, Acc &acc,
+  __device__ __forceinline__ static void scalar(const unsigned char *xb, uint64_t i,
+                                                const unsigned char *yb, uint64_t j,
+                                                Acc &acc,
                                                 const unsigned char *smem) {
     const T *tab = reinterpret_cast<const T *>(smem);
     acc.mac_d(0, static_cast<double>(multiply(load_code<16, 16>(xb, i),
-                                              load_code<16, 16>(yb, i), tab)),
+                                              load_code<16, 16>(yb, j), tab)),
               1.0);
   }
 };
@@ -504,13 +509,13 @@ __device__ __forceinline__ void flush_tile(Acc &acc, float *lanes) {
 }
 
 template <class Codec, class Acc>
-__device__ __forceinline__ void ragged_tail(const unsigned char *xb,
-                                            const unsigned char *yb,
+__device__ __forceinline__ void ragged_tail(const unsigned char *xb, uint64_t xo,
+                                            const unsigned char *yb, uint64_t yo,
                                             uint64_t first, uint64_t n,
                                             Acc &acc, const unsigned char *smem) {
   for (uint64_t i = first + static_cast<uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
        i < n; i += static_cast<uint64_t>(gridDim.x) * kThreads)
-    Codec::scalar(xb, yb, i, acc, smem);
+    Codec::scalar(xb, xo + i, yb, yo + i, acc, smem);
 }
 
 // ---------------------------------------------------------------------------
@@ -528,8 +533,10 @@ __global__ void __launch_bounds__(kThreads)
   constexpr uint64_t tile_packets = static_cast<uint64_t>(kThreads) * U;
 
   const unsigned int batch = blockIdx.y;
-  const unsigned char *xb = p.x + batch * p.batch_stride;
-  const unsigned char *yb = p.y + batch * p.batch_stride;
+  const unsigned char *xb = p.x + batch * p.x_stride;
+  const unsigned char *yb = p.y + batch * p.y_stride;
+  const uint64_t xo = p.x_first + batch * p.x_index_stride;
+  const uint64_t yo = p.y_first + batch * p.y_index_stride;
 
   if constexpr (Codec::kTableBytes > 0) {
     Codec::prepare(p.table, smem);
@@ -560,7 +567,7 @@ __global__ void __launch_bounds__(kThreads)
     flush_tile<Codec>(acc, lanes);
   }
 
-  ragged_tail<Codec>(xb, yb, tiles * tile_packets * P, p.n, acc, smem);
+  ragged_tail<Codec>(xb, xo, yb, yo, tiles * tile_packets * P, p.n, acc, smem);
   const double s = block_sum(acc.value(), scratch);
   grid_finish(s, p.partials + static_cast<uint64_t>(batch) * gridDim.x,
               p.tickets + batch, p.results + batch, scratch);
@@ -661,8 +668,10 @@ __global__ void __launch_bounds__(kThreads)
   __shared__ __align__(8) uint64_t full[STAGES];
 
   const unsigned int batch = blockIdx.y;
-  const unsigned char *xb = p.x + batch * p.batch_stride;
-  const unsigned char *yb = p.y + batch * p.batch_stride;
+  const unsigned char *xb = p.x + batch * p.x_stride;
+  const unsigned char *yb = p.y + batch * p.y_stride;
+  const uint64_t xo = p.x_first + batch * p.x_index_stride;
+  const uint64_t yo = p.y_first + batch * p.y_index_stride;
   unsigned char *ring = smem + Codec::kTableBytes;
 
   const uint64_t tiles = p.vector_ok ? p.n / shape::TILE_VALUES : 0;
@@ -735,7 +744,7 @@ __global__ void __launch_bounds__(kThreads)
     }
     __syncthreads();
   } else {
-    ragged_tail<Codec>(xb, yb, tiles * shape::TILE_VALUES, p.n, acc, smem);
+    ragged_tail<Codec>(xb, xo, yb, yo, tiles * shape::TILE_VALUES, p.n, acc, smem);
   }
   const double mine_sum = failed ? __longlong_as_double(0x7ff8000000000000ll) : acc.value();
   const double s = block_sum(mine_sum, scratch);
@@ -916,10 +925,36 @@ int32_t dot_supported(int32_t format, int32_t layout, int32_t accum) {
   return lookup(format, layout, accum, AUT_STRATEGY_AUTO).fn != nullptr ? 1 : 0;
 }
 
+// The vector paths need 16-byte aligned streams for every pair of the batch.
+static bool vector_path_ok(const void *x, const void *y, uint32_t batch, const batch_layout &bl) {
+  const bool bases = reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(y) % 16 == 0;
+  if (batch <= 1) return bases;
+  return bases && bl.x_stride % 16 == 0 && bl.y_stride % 16 == 0 &&
+         bl.x_index_stride == 0 && bl.y_index_stride == 0;
+}
+
+// Kernel parameters for the pairs b0, b0 + 1, ... of a batch.
+static aut::dev::dot_params params_for(const void *x, const void *y, uint64_t n, uint32_t b0,
+                                const batch_layout &bl, bool aligned) {
+  aut::dev::dot_params p{};
+  p.x = static_cast<const unsigned char *>(x) + static_cast<uint64_t>(b0) * bl.x_stride;
+  p.y = static_cast<const unsigned char *>(y) + static_cast<uint64_t>(b0) * bl.y_stride;
+  p.x_stride = bl.x_stride;
+  p.y_stride = bl.y_stride;
+  p.x_first = static_cast<uint64_t>(b0) * bl.x_index_stride;
+  p.y_first = static_cast<uint64_t>(b0) * bl.y_index_stride;
+  p.x_index_stride = bl.x_index_stride;
+  p.y_index_stride = bl.y_index_stride;
+  p.n = n;
+  p.vector_ok = aligned ? 1 : 0;
+  return p;
+}
+
 aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
                       int32_t accum, int32_t strategy, int32_t decoder,
                       const void *x, const void *y, uint64_t n, uint32_t batch,
-                      uint64_t batch_stride, double *results, void *stream,
+                      const batch_layout &bl, double *results, void *stream,
                       double *partials, unsigned int *tickets,
                       unsigned int *status, int max_blocks_total) {
   // SCALAR runs the LDG kernel with the vector path switched off, so every
@@ -944,10 +979,7 @@ aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
                                 : static_cast<const void *>(t->frac_f64);
   }
 
-  const bool aligned = !scalar_only &&
-                       (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
-                       (reinterpret_cast<uintptr_t>(y) % 16 == 0) &&
-                       (batch <= 1 || batch_stride % 16 == 0);
+  const bool aligned = !scalar_only && vector_path_ok(x, y, batch, bl);
   const int cap = ws->sm_count * e.blocks_per_sm;
   uint64_t wanted = aligned ? (n / e.tile_values) : 0;
   if (wanted == 0) wanted = (n + aut::dev::kThreads - 1) / aut::dev::kThreads;
@@ -960,12 +992,7 @@ aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
     if (per_pair < 1) per_pair = 1;
     if (static_cast<uint64_t>(per_pair) > wanted) per_pair = static_cast<int>(wanted);
     if (per_pair > max_blocks_total) per_pair = max_blocks_total;
-    aut::dev::dot_params p;
-    p.x = static_cast<const unsigned char *>(x) + static_cast<uint64_t>(b0) * batch_stride;
-    p.y = static_cast<const unsigned char *>(y) + static_cast<uint64_t>(b0) * batch_stride;
-    p.n = n;
-    p.batch_stride = batch_stride;
-    p.vector_ok = aligned ? 1 : 0;
+    aut::dev::dot_params p = params_for(x, y, n, b0, bl, aligned);
     p.table = table;
     p.partials = partials;
     p.tickets = tickets;
@@ -984,7 +1011,7 @@ aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
 // nothing is allocated.
 aut_status dot_launch_scratch(int sm_count, int32_t format, int32_t layout,
                               int32_t accum, const void *x, const void *y,
-                              uint64_t n, uint32_t batch, uint64_t batch_stride,
+                              uint64_t n, uint32_t batch, const batch_layout &bl,
                               double *results, void *stream, double *partials,
                               unsigned int *tickets, unsigned int *status,
                               int slots) {
@@ -997,9 +1024,7 @@ aut_status dot_launch_scratch(int sm_count, int32_t format, int32_t layout,
                 "this format decodes through tables kept in a workspace; use aut_dot");
   aut_status st = blocks_per_sm(e);
   if (st != AUT_OK) return st;
-  const bool aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
-                       (reinterpret_cast<uintptr_t>(y) % 16 == 0) &&
-                       (batch <= 1 || batch_stride % 16 == 0);
+  const bool aligned = vector_path_ok(x, y, batch, bl);
   uint64_t wanted = aligned ? (n / e.tile_values) : 0;
   if (wanted == 0) wanted = (n + aut::dev::kThreads - 1) / aut::dev::kThreads;
   if (wanted == 0) wanted = 1;
@@ -1009,12 +1034,7 @@ aut_status dot_launch_scratch(int sm_count, int32_t format, int32_t layout,
   if (per_pair > cap) per_pair = cap;
   if (static_cast<uint64_t>(per_pair) > wanted) per_pair = static_cast<int>(wanted);
   if (per_pair < 1) per_pair = 1;
-  aut::dev::dot_params p;
-  p.x = static_cast<const unsigned char *>(x);
-  p.y = static_cast<const unsigned char *>(y);
-  p.n = n;
-  p.batch_stride = batch_stride;
-  p.vector_ok = aligned ? 1 : 0;
+  aut::dev::dot_params p = params_for(x, y, n, 0, bl, aligned);
   p.table = nullptr;
   p.partials = partials;
   p.tickets = tickets;

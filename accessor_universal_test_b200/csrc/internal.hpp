@@ -50,6 +50,16 @@ struct lns_tables {
 };
 
 constexpr int kMaxBatchPerLaunch = 1024;
+
+// Where the pairs of a batched launch live: pair b reads x at byte
+// b * x_stride and value index x_first + b * x_index_stride (and likewise y).
+// Byte strides serve pairs that start on 16-byte boundaries (the vector
+// paths); value-index strides serve rows of a dense matrix that start inside
+// a byte or word, which the per-value path reads by absolute index.
+struct batch_layout {
+  uint64_t x_stride = 0, y_stride = 0;
+  uint64_t x_index_stride = 0, y_index_stride = 0;
+};
 constexpr int kLnsFormatsCached = 8;
 
 } // namespace aut::lib

@@ -16,7 +16,7 @@ namespace aut::lib {
 aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
                       int32_t accum, int32_t strategy, int32_t decoder,
                       const void *x, const void *y, uint64_t n, uint32_t batch,
-                      uint64_t batch_stride, double *results, void *stream,
+                      const batch_layout &bl, double *results, void *stream,
                       double *partials, unsigned int *tickets,
                       unsigned int *status, int max_blocks_total);
 int32_t dot_supported(int32_t format, int32_t layout, int32_t accum);
@@ -549,8 +549,8 @@ aut_status aut_dot_variant(aut_workspace *ws, int32_t format, int32_t layout,
     return fail(AUT_ERR_INVALID_ARGUMENT, "unknown decoder");
   device_scope scope(ws->device);
   AUT_CUDA_TRY(scope.err);
-  return dot_launch(ws, format, layout, accum, strategy, decoder, x, y, n, 1, 0,
-                    result, stream, ws->partials, ws->tickets,
+  return dot_launch(ws, format, layout, accum, strategy, decoder, x, y, n, 1,
+                    batch_layout{}, result, stream, ws->partials, ws->tickets,
                     ws->tickets + kMaxBatchPerLaunch, ws->max_blocks);
 }
 
@@ -567,10 +567,47 @@ aut_status aut_dot_batched(aut_workspace *ws, int32_t format, int32_t layout,
     return fail(AUT_ERR_INVALID_ARGUMENT, "batch stride smaller than one vector");
   device_scope scope(ws->device);
   AUT_CUDA_TRY(scope.err);
+  batch_layout bl;
+  bl.x_stride = bl.y_stride = batch_stride_bytes;
   return dot_launch(ws, format, layout, accum, AUT_STRATEGY_AUTO,
-                    AUT_DECODER_AUTO, x, y, n, batch, batch_stride_bytes,
+                    AUT_DECODER_AUTO, x, y, n, batch, bl,
                     results, stream, ws->partials,
                     ws->tickets, ws->tickets + kMaxBatchPerLaunch,
+                    ws->max_blocks);
+}
+
+aut_status aut_gemv(aut_workspace *ws, int32_t format, int32_t layout,
+                    int32_t accum, int32_t strategy, int32_t decoder,
+                    const void *matrix, const void *vector, uint64_t rows,
+                    uint64_t columns, double *result, void *stream) {
+  clear_error();
+  aut_status st = check_dot_args(ws, format, layout, accum, matrix, vector,
+                                 rows == 0 ? 0 : columns, result);
+  if (st != AUT_OK) return st;
+  if (strategy < AUT_STRATEGY_AUTO || strategy > AUT_STRATEGY_SCALAR)
+    return fail(AUT_ERR_INVALID_ARGUMENT, "unknown access strategy");
+  if (decoder < AUT_DECODER_AUTO || decoder > AUT_DECODER_FRACTION_LUT_FUSED)
+    return fail(AUT_ERR_INVALID_ARGUMENT, "unknown decoder");
+  if (rows == 0) return AUT_OK;
+  if (rows > 0xffffffffull)
+    return fail(AUT_ERR_TOO_LARGE, "at most 2^32 - 1 rows per call");
+  const uint64_t bits = static_cast<uint64_t>(stride_bits(*find_format(format), layout));
+  if (columns > (uint64_t{1} << 56) / bits / rows)
+    return fail(AUT_ERR_TOO_LARGE, "matrix larger than 2^53 bytes");
+  // Row r is the DOT of values [r * columns, (r + 1) * columns) of the matrix
+  // stream with the vector: rows that start on 16-byte boundaries are read by
+  // byte stride on the vector paths, the others by absolute value index.
+  batch_layout bl;
+  const uint64_t row_bits = columns * bits;
+  if (row_bits % 128 == 0)
+    bl.x_stride = row_bits / 8;
+  else
+    bl.x_index_stride = columns;
+  device_scope scope(ws->device);
+  AUT_CUDA_TRY(scope.err);
+  return dot_launch(ws, format, layout, accum, strategy, decoder, matrix, vector,
+                    columns, static_cast<uint32_t>(rows), bl, result, stream,
+                    ws->partials, ws->tickets, ws->tickets + kMaxBatchPerLaunch,
                     ws->max_blocks);
 }
 

@@ -75,7 +75,7 @@ void set_up(device_setup &s, int device) {
 namespace aut::lib {
 aut_status dot_launch_scratch(int sm_count, int32_t format, int32_t layout,
                               int32_t accum, const void *x, const void *y,
-                              uint64_t n, uint32_t batch, uint64_t batch_stride,
+                              uint64_t n, uint32_t batch, const batch_layout &bl,
                               double *results, void *stream, double *partials,
                               unsigned int *tickets, unsigned int *status,
                               int slots);
@@ -121,8 +121,10 @@ extern "C" aut_status aut_dot_noalloc(int32_t format, int32_t layout,
   AUT_CUDA_TRY(cudaMemsetAsync(s.scratch->tickets, 0,
                                sizeof(s.scratch->tickets) + sizeof(s.scratch->status),
                                static_cast<cudaStream_t>(stream)));
+  batch_layout bl;
+  bl.x_stride = bl.y_stride = batch_stride_bytes;
   return dot_launch_scratch(s.sm_count, format, layout, accum, x, y, n, batch,
-                            batch_stride_bytes, results, stream,
+                            bl, results, stream,
                             s.scratch->partials, s.scratch->tickets,
                             &s.scratch->status, kSlots);
 }

@@ -192,6 +192,22 @@ aut_status aut_dot_batched(aut_workspace *ws, int32_t format, int32_t layout,
                            uint64_t batch_stride_bytes, double *results,
                            void *stream);
 
+/* Matrix-vector product over compact storage, the reference's other kernel
+ * (gemv_thread_kernel, bitwidth_benchmark_kernels.cuh:459-501; raw FP32/FP64
+ * raw_gemv_kernel, :705-728):
+ *   result[r] = sum_c decode(matrix[r * columns + c]) * decode(vector[c])
+ * for r < rows, written to device memory as FP64.  The matrix is one stream
+ * of rows * columns values in `layout` (row-major), the vector one stream of
+ * `columns` values, both in `format`.  Each row is a fused DOT of the same
+ * kernels as aut_dot_variant; when columns * bits-per-slot is a multiple of
+ * 128 every row starts on a 16-byte boundary and takes the vectorised path,
+ * otherwise rows are read value by value.  rows = 0 does nothing; columns =
+ * 0 writes zeros. */
+aut_status aut_gemv(aut_workspace *ws, int32_t format, int32_t layout,
+                    int32_t accum, int32_t strategy, int32_t decoder,
+                    const void *matrix, const void *vector, uint64_t rows,
+                    uint64_t columns, double *result, void *stream);
+
 /* The fused DOT without a workspace, for callers that cannot allocate device
  * memory (a host framework that owns the GPU's memory through its own pool,
  * a latency-critical path that cannot absorb cudaMalloc's device-wide
