@@ -7,7 +7,11 @@
 // of one binary per width, the access strategies are this library's
 // (scalar / thread_packet = LDG / tma_bulk = TMA), data come from the seeded
 // generators of aut_generate (uniform_0_1: (0,1]; normal_0_1: Irwin-Hall)
-// instead of cuRAND, and GEMV rows are not produced (--gemv-* are accepted).
+// instead of cuRAND.  GEMV rows (kernel "gemv", --gemv-powers / --gemv-rows,
+// src/bitwidth_strategy_bench.cu:653-684) time aut_gemv over the same
+// strategies and decoders.  The scalar rows (one value per thread, AUTO
+// decoder) carry the decoder names the reference's smoke validators take as
+// their baseline: "generic" (bitwidth) and "reference_exp2" (LNS).
 #include <autdot.h>
 
 #include <cuda_runtime.h>
@@ -53,6 +57,8 @@ struct options {
   std::vector<std::string> formats;
   std::string mode{"screen"};
   std::vector<int> dot_powers{24};
+  std::vector<int> gemv_powers{14};
+  uint64_t gemv_rows{1024};
   std::vector<std::string> distributions{"uniform_0_1", "normal_0_1"};
   std::vector<std::string> accums{"fp32", "fp64"};
   int warmup{5};
@@ -77,7 +83,10 @@ options parse(int argc, char **argv) {
     else if (a == "--dot-powers") {
       o.dot_powers.clear();
       for (auto &t : split(value())) o.dot_powers.push_back(std::stoi(t));
-    } else if (a == "--gemv-powers" || a == "--gemv-rows") value();
+    } else if (a == "--gemv-powers") {
+      o.gemv_powers.clear();
+      for (auto &t : split(value())) o.gemv_powers.push_back(std::stoi(t));
+    } else if (a == "--gemv-rows") o.gemv_rows = std::stoull(value());
     else if (a == "--distributions") o.distributions = split(value());
     else if (a == "--accums") o.accums = split(value());
     else if (a == "--warmup") o.warmup = std::stoi(value());
@@ -94,7 +103,8 @@ options parse(int argc, char **argv) {
         if (!line.empty() && line[0] != '#') o.variants.insert(line);
     } else if (a == "--help" || a == "-h") {
       std::cout << "strategy_bench --family bitwidth|lns --formats e2m3,e8m0,... "
-                   "--mode smoke|screen|full --dot-powers 24 --distributions "
+                   "--mode smoke|screen|full --dot-powers 24 --gemv-powers 14 "
+                   "--gemv-rows 1024 --distributions "
                    "uniform_0_1,normal_0_1 --accums fp32,fp64 --warmup N --samples N "
                    "--target-sample-ms X --seed N --output PATH [--variants a,b] "
                    "[--variant-file PATH]\n";
@@ -111,6 +121,8 @@ options parse(int argc, char **argv) {
     o.output = o.family == "lns" ? "lns_timing_samples.csv" : "timing_samples.csv";
   if (o.mode == "smoke") {  // the reference's smoke overrides
     o.dot_powers = {12};
+    o.gemv_powers = {8};
+    o.gemv_rows = 32;
     o.warmup = 1;
     o.samples = 1;
     o.target_sample_ms = 0.0;
@@ -143,12 +155,28 @@ struct access {
   const char *redistribution;
 };
 
-const char *decoder_name(const std::string &family, const std::string &fmt, bool scalar) {
-  if (scalar) return family == "lns" ? "reference_exp2" : "generic";
-  if (fmt == "e2m3") return "native_packed";
-  if (fmt == "lns8_r3") return "full_lut_shared";
-  if (fmt == "lns16_r11") return "fraction_lut_shared";
-  return "direct_shift";
+// The decoders this library has for a format and accumulator, with the
+// reference's decoder_kind / multiply_kind names (lns_decoder_strategies.cuh:19-36).
+struct decoder_choice {
+  int32_t id;
+  const char *name;
+  const char *multiply;  // LNS only
+  int table_bytes;       // shared-memory table per block
+};
+
+std::vector<decoder_choice> decoders_for(const std::string &fmt, int32_t accum) {
+  const int t = accum == AUT_ACCUM_FP64 ? 8 : 4;
+  if (fmt == "lns8_r3") return {{AUT_DECODER_FULL_LUT, "full_lut_shared", "ordinary", 256 * 32 * t}};
+  if (fmt == "lns16_r11") {
+    std::vector<decoder_choice> d;
+    if (accum == AUT_ACCUM_FP32)
+      d.push_back({AUT_DECODER_FULL_LUT, "full_lut_shared", "ordinary", 32768 * 4});
+    d.push_back({AUT_DECODER_FRACTION_LUT, "fraction_lut_shared", "ordinary", 2048 * t});
+    d.push_back({AUT_DECODER_FRACTION_LUT_FUSED, "fraction_lut_shared", "fused", 2048 * t});
+    return d;
+  }
+  if (fmt == "e2m3") return {{AUT_DECODER_DIRECT, "native_packed", "ordinary", 0}};
+  return {{AUT_DECODER_DIRECT, "direct_shift", "ordinary", 0}};
 }
 
 } // namespace
@@ -198,8 +226,34 @@ int main(int argc, char **argv) {
                                {"thread_packet", AUT_STRATEGY_LDG, "none"},
                                {"tma_bulk", AUT_STRATEGY_TMA, "tma_bulk_shared"}};
     const int max_power = *std::max_element(o.dot_powers.begin(), o.dot_powers.end());
-    const uint64_t max_n = uint64_t{1} << max_power;
+    uint64_t max_n = uint64_t{1} << max_power;
+    for (int p : o.gemv_powers)
+      max_n = std::max(max_n, (o.gemv_rows + 1) << p);
     device_buffer values(max_n * sizeof(double));
+    device_buffer gemv_out(o.gemv_rows * sizeof(double));
+
+    // Times `launch` (warm-up, a pilot to size samples of target_sample_ms,
+    // then `samples` samples) and returns (iterations, per-sample ms).
+    auto measure = [&](const auto &launch) {
+      auto timed = [&](int iters) {
+        cuda_check(cudaEventRecord(start), "record");
+        for (int k = 0; k < iters; ++k) launch();
+        cuda_check(cudaEventRecord(stop), "record");
+        cuda_check(cudaEventSynchronize(stop), "sync");
+        float ms = 0.f;
+        cuda_check(cudaEventElapsedTime(&ms, start, stop), "elapsed");
+        return static_cast<double>(ms);
+      };
+      for (int w = 0; w < o.warmup; ++w) launch();
+      cuda_check(cudaDeviceSynchronize(), "warmup");
+      const double pilot = timed(1);
+      int iterations = 1;
+      if (o.target_sample_ms > 0 && pilot > 0)
+        iterations = std::clamp(static_cast<int>(std::ceil(o.target_sample_ms / pilot)), 1, 10000);
+      std::vector<double> times;
+      for (int k = 0; k < o.samples; ++k) times.push_back(timed(iterations));
+      return std::make_pair(iterations, times);
+    };
 
     for (size_t d = 0; d < o.distributions.size(); ++d) {
       const std::string &dist = o.distributions[d];
@@ -215,6 +269,12 @@ int main(int argc, char **argv) {
         int32_t family = 0, bits = 0, ebits = 0, finite = 0;
         aut_format_info(fid, &family, &bits, &ebits, &finite);
         aut_check(aut_workspace_prepare(ws, fid), "aut_workspace_prepare");
+        auto encode = [&](uint64_t vector_id, uint64_t n, int32_t layout, void *dst) {
+          aut_check(aut_generate(kind, seed, vector_id, 0, n, static_cast<double *>(values.p), nullptr),
+                    "generate");
+          aut_check(aut_encode(ws, fid, layout, static_cast<double *>(values.p), n, dst, nullptr),
+                    "encode");
+        };
         for (const auto &acc_name : o.accums) {
           const int32_t accum = acc_name == "fp64" ? AUT_ACCUM_FP64 : AUT_ACCUM_FP32;
           std::cout << "  " << name << " -> " << acc_name << "\n";
@@ -222,82 +282,105 @@ int main(int argc, char **argv) {
             if (!aut_dot_supported(fid, layout, accum)) continue;
             const int stride = layout == AUT_LAYOUT_DENSE ? bits
                                : bits <= 8 ? 8 : bits <= 16 ? 16 : 32;
-            for (int power : o.dot_powers) {
-              const uint64_t n = uint64_t{1} << power;
-              device_buffer xs(aut_storage_bytes(fid, layout, n));
-              device_buffer ys(aut_storage_bytes(fid, layout, n));
-              aut_check(aut_generate(kind, seed, 0, 0, n, static_cast<double *>(values.p), nullptr), "generate");
-              aut_check(aut_encode(ws, fid, layout, static_cast<double *>(values.p), n, xs.p, nullptr), "encode");
-              aut_check(aut_generate(kind, seed, 1, 0, n, static_cast<double *>(values.p), nullptr), "generate");
-              aut_check(aut_encode(ws, fid, layout, static_cast<double *>(values.p), n, ys.p, nullptr), "encode");
-              cuda_check(cudaDeviceSynchronize(), "encode");
-              for (const access &ac : accesses) {
-                const bool scalar = ac.strategy == AUT_STRATEGY_SCALAR;
-                const char *dec = decoder_name(o.family, name, scalar);
-                const int packet = scalar ? 1
-                                   : ac.strategy == AUT_STRATEGY_LDG
-                                       ? 128 * (stride / gcd_int(stride, 128)) / stride
-                                       : (stride >= 24 ? 16 : 32);
+            auto physical_bytes = [&](uint64_t count) {
+              return layout == AUT_LAYOUT_DENSE ? (count * bits + 7) / 8 : count * (stride / 8);
+            };
+            // One CSV row per sample (the reference's schema).
+            auto emit = [&](const char *kernel, const access &ac, const decoder_choice &dc,
+                            int packet, const std::string &id, uint64_t n, uint64_t m,
+                            uint64_t rows, double logical, uint64_t physical, uint64_t blocks,
+                            int iterations, const std::vector<double> &times, double result,
+                            int valid) {
+              for (size_t k = 0; k < times.size(); ++k) {
+                csv << stamp << ',' << prop.name << ',' << o.mode << ',' << dist << ','
+                    << kernel << ',';
+                if (o.family == "lns")
+                  csv << "lns," << name << ',' << bits << ',' << (bits - 1 - ebits) << ','
+                      << ebits << ',' << acc_name << ',' << dc.multiply << ',';
+                else
+                  csv << name << ',' << bits << ',' << ebits << ',' << (bits - 1 - ebits)
+                      << ',' << acc_name << ',';
+                csv << (layout == AUT_LAYOUT_DENSE ? "dense" : "padded") << ',' << ac.name
+                    << ',' << packet << ',' << (layout == AUT_LAYOUT_DENSE ? 32 : stride)
+                    << ",1," << (ac.strategy == AUT_STRATEGY_TMA ? 256 : 1) << ',' << packet
+                    << ',' << ac.redistribution << ',' << dc.name << ',' << id << ',' << n
+                    << ',' << m << ',' << rows << ',' << logical << ',' << physical << ','
+                    << dc.table_bytes << ',' << blocks << ",256," << o.warmup << ',' << k
+                    << ',' << iterations << ',' << times[k] << ',' << times[k] / iterations
+                    << ',' << std::setprecision(17) << result << std::setprecision(6) << ','
+                    << valid << '\n';
+              }
+            };
+            auto status_ok = [&] {
+              uint32_t status = 0;
+              aut_check(aut_workspace_status(ws, &status, 1), "status");
+              return status == 0;
+            };
+            for (const access &ac : accesses) {
+              const bool scalar = ac.strategy == AUT_STRATEGY_SCALAR;
+              const int packet = scalar ? 1
+                                 : ac.strategy == AUT_STRATEGY_LDG
+                                     ? 128 * (stride / gcd_int(stride, 128)) / stride
+                                     : (stride >= 24 ? 16 : 32);
+              std::vector<decoder_choice> choices = decoders_for(name, accum);
+              if (scalar) {
+                // the validators' baseline row: one per format and accumulator
+                decoder_choice base = choices.back();
+                if (name == "lns16_r11") base = choices[accum == AUT_ACCUM_FP32 ? 1 : 0];
+                base.id = AUT_DECODER_AUTO;
+                base.name = o.family == "lns" ? "reference_exp2" : "generic";
+                base.multiply = "ordinary";
+                choices = {base};
+              }
+              for (const decoder_choice &dc : choices) {
                 std::ostringstream id;
-                if (o.family == "lns") id << "ordinary/";
+                if (o.family == "lns") id << dc.multiply << '/';
                 id << (layout == AUT_LAYOUT_DENSE ? "dense" : "padded") << '/' << ac.name
-                   << "/x" << packet << '/' << dec;
+                   << "/x" << packet << '/' << dc.name;
                 const std::string qualified = name + "/" + acc_name + "/" + id.str();
                 if (!o.variants.empty() && !o.variants.count(id.str()) &&
                     !o.variants.count(qualified))
                   continue;
-                auto launch = [&] {
-                  aut_check(aut_dot_strategy(ws, fid, layout, accum, ac.strategy, xs.p, ys.p, n,
-                                             d_result, nullptr),
-                            "aut_dot_strategy");
-                };
-                auto timed = [&](int iters) {
-                  cuda_check(cudaEventRecord(start), "record");
-                  for (int k = 0; k < iters; ++k) launch();
-                  cuda_check(cudaEventRecord(stop), "record");
-                  cuda_check(cudaEventSynchronize(stop), "sync");
-                  float ms = 0.f;
-                  cuda_check(cudaEventElapsedTime(&ms, start, stop), "elapsed");
-                  return static_cast<double>(ms);
-                };
-                for (int w = 0; w < o.warmup; ++w) launch();
-                cuda_check(cudaDeviceSynchronize(), "warmup");
-                const double pilot = timed(1);
-                int iterations = 1;
-                if (o.target_sample_ms > 0 && pilot > 0)
-                  iterations = std::clamp(static_cast<int>(std::ceil(o.target_sample_ms / pilot)), 1, 10000);
-                std::vector<double> times;
-                for (int s = 0; s < o.samples; ++s) times.push_back(timed(iterations));
-                double result = 0.0;
-                cuda_check(cudaMemcpy(&result, d_result, sizeof result, cudaMemcpyDeviceToHost), "copy");
-                uint32_t status = 0;
-                aut_check(aut_workspace_status(ws, &status, 1), "status");
-                const int valid = std::isfinite(result) && status == 0 ? 1 : 0;
-                const double logical = 2.0 * n * bits / 8.0;
-                const uint64_t physical = 2 * (layout == AUT_LAYOUT_DENSE
-                                                   ? (n * bits + 7) / 8
-                                                   : n * (stride / 8));
-                const int table = name == "lns8_r3" ? 256 * (accum == AUT_ACCUM_FP64 ? 8 : 4)
-                                  : name == "lns16_r11" ? 2048 * (accum == AUT_ACCUM_FP64 ? 8 : 4)
-                                                        : 0;
-                for (size_t s = 0; s < times.size(); ++s) {
-                  csv << stamp << ',' << prop.name << ',' << o.mode << ',' << dist << ",dot,";
-                  if (o.family == "lns")
-                    csv << "lns," << name << ',' << bits << ',' << (bits - 1 - ebits) << ','
-                        << ebits << ',' << acc_name << ",ordinary,";
-                  else
-                    csv << name << ',' << bits << ',' << ebits << ',' << (bits - 1 - ebits)
-                        << ',' << acc_name << ',';
-                  csv << (layout == AUT_LAYOUT_DENSE ? "dense" : "padded") << ',' << ac.name
-                      << ',' << packet << ',' << (layout == AUT_LAYOUT_DENSE ? 32 : stride)
-                      << ',' << (ac.strategy == AUT_STRATEGY_TMA ? 1 : 1) << ','
-                      << (ac.strategy == AUT_STRATEGY_TMA ? 256 : 1) << ',' << packet << ','
-                      << ac.redistribution << ',' << dec << ',' << id.str() << ',' << n
-                      << ",0,1," << logical << ',' << physical << ',' << table << ','
-                      << max_blocks << ",256," << o.warmup << ',' << s << ',' << iterations
-                      << ',' << times[s] << ',' << times[s] / iterations << ','
-                      << std::setprecision(17) << result << std::setprecision(6) << ','
-                      << valid << '\n';
+                for (int power : o.dot_powers) {
+                  const uint64_t n = uint64_t{1} << power;
+                  device_buffer xs(aut_storage_bytes(fid, layout, n));
+                  device_buffer ys(aut_storage_bytes(fid, layout, n));
+                  encode(0, n, layout, xs.p);
+                  encode(1, n, layout, ys.p);
+                  cuda_check(cudaDeviceSynchronize(), "encode");
+                  const auto [iterations, times] = measure([&] {
+                    aut_check(aut_dot_variant(ws, fid, layout, accum, ac.strategy, dc.id, xs.p,
+                                              ys.p, n, d_result, nullptr),
+                              "aut_dot_variant");
+                  });
+                  double result = 0.0;
+                  cuda_check(cudaMemcpy(&result, d_result, sizeof result, cudaMemcpyDeviceToHost),
+                             "copy");
+                  const int valid = std::isfinite(result) && status_ok() ? 1 : 0;
+                  emit("dot", ac, dc, packet, id.str(), n, 0, 1, 2.0 * n * bits / 8.0,
+                       2 * physical_bytes(n), max_blocks, iterations, times, result, valid);
+                }
+                for (int power : o.gemv_powers) {
+                  const uint64_t columns = uint64_t{1} << power;
+                  const uint64_t rows = o.gemv_rows;
+                  device_buffer ms(aut_storage_bytes(fid, layout, rows * columns));
+                  device_buffer vs(aut_storage_bytes(fid, layout, columns));
+                  encode(0, rows * columns, layout, ms.p);
+                  encode(1, columns, layout, vs.p);
+                  cuda_check(cudaDeviceSynchronize(), "encode");
+                  double *out = static_cast<double *>(gemv_out.p);
+                  const auto [iterations, times] = measure([&] {
+                    aut_check(aut_gemv(ws, fid, layout, accum, ac.strategy, dc.id, ms.p, vs.p,
+                                       rows, columns, out, nullptr),
+                              "aut_gemv");
+                  });
+                  double first = 0.0;
+                  cuda_check(cudaMemcpy(&first, out, sizeof first, cudaMemcpyDeviceToHost), "copy");
+                  const int valid = std::isfinite(first) && status_ok() ? 1 : 0;
+                  const uint64_t count = rows * columns + columns;
+                  emit("gemv", ac, dc, packet, id.str(), columns, rows, rows,
+                       static_cast<double>(count) * bits / 8.0, physical_bytes(count), rows,
+                       iterations, times, first, valid);
                 }
                 if (o.mode == "smoke") std::cout << "    " << qualified << "\n";
               }

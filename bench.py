@@ -2,7 +2,7 @@
 """Benchmark of the decode-fused DOT library (libautdot, sm_100a).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload e8-sweep|e2m3|lns|raw] [--accum fp32|fp64]
+                    [--workload e8-sweep|e2m3|lns|raw|gemv] [--accum fp32|fp64]
 
 Default workload (the one the headline metric is quoted on): the E8
 truncated-float bit-width sweep -- e8m0 (9 bits; the 8-bit width has no room
@@ -21,6 +21,10 @@ e2e      the same metric through the C ABI from pinned HOST buffers: every
          the FP64 results back.
 roofline the dominant kernel's packed bytes per launch / its CUDA-event
          launch time, against the measured HBM copy bandwidth.
+
+The gemv workload runs aut_gemv instead: a 1024-row matrix of the E8 sweep
+formats with N / 1024 columns per GPU (rows sharded over GPUs, no
+collective), packed bytes = (rows * columns + columns) * bits / 8.
 """
 from __future__ import annotations
 
@@ -52,7 +56,12 @@ WORKLOADS = {
             [("lns8_r3", 3), ("lns16_r11", 3)], 0, 1 << 28),
     "raw": ("raw FP32 and FP64 storage DOT, x,y uniform[-1,1)",
             [("fp32", 1), ("fp64", 0)], 0, N_DEFAULT),
+    "gemv": ("GEMV over the E8 sweep formats: 1024 x N/1024 matrix per GPU times a dense "
+             "vector of the same format, uniform[-1,1)",
+             [("e8m0", 0), ("e8m1", 0), ("e8m3", 0), ("e8m5", 0), ("bf16_e8m7", 0),
+              ("e8m15", 0)], 0, N_DEFAULT),
 }
+GEMV_ROWS = 1024
 METRIC = "decoded elems/s & HBM GB/s (% of 8 TB/s) at N=2^27/GPU, 1-8 GPUs; normalized err"
 
 
@@ -263,6 +272,14 @@ def run_reference_arm(args, rank, world):
 
 def config_of(args, world, desc, n_full):
     n = args.n or n_full
+    if args.workload == "gemv":
+        return {"workload": f"{desc}; {GEMV_ROWS} x {n // GEMV_ROWS} per GPU", "n_per_gpu": n,
+                "rows": GEMV_ROWS, "columns": n // GEMV_ROWS,
+                "formats": [f for f, _ in WORKLOADS[args.workload][1]],
+                "layout": "dense", "accumulator": args.accum,
+                "l2": "matrices larger than L2 (each > 126 MB); the vector is re-read from "
+                      "L2 by every row",
+                "parallelism": f"rows sharded x{world}, no collective"}
     return {"workload": f"{desc}; N={n} per GPU", "n_per_gpu": n,
             "formats": [f for f, _ in WORKLOADS[args.workload][1]],
             "layout": "dense", "accumulator": args.accum,
@@ -296,25 +313,39 @@ def main():
     ws = _lib.Workspace(local)
     strategy = {"auto": 0, "ldg": 1, "tma": 2}[args.strategy]
     stream = torch.cuda.current_stream().cuda_stream
+    gemv = args.workload == "gemv"
+    rows = GEMV_ROWS if gemv else 1      # results per format
+    cols = n // rows                     # values per DOT
     fids, inputs, packed_bytes = [], [], []
     for name, kind in fmts:
         fid = _lib.format_id(name)
         ws.prepare(fid)
-        x = vectors.encoded(ws, fid, layout, kind, SEED, 0, n, first=rank * n)
-        y = vectors.encoded(ws, fid, layout, kind, SEED, 1, n, first=rank * n)
+        x = vectors.encoded(ws, fid, layout, kind, SEED, 0, rows * cols, first=rank * rows * cols)
+        if gemv:  # the same vector on every GPU
+            y = vectors.encoded(ws, fid, layout, kind, SEED, 1, cols)
+        else:
+            y = vectors.encoded(ws, fid, layout, kind, SEED, 1, n, first=rank * n)
         fids.append(fid)
         inputs.append((x, y))
-        packed_bytes.append(2 * n * _lib.format_info(fid)[1] / 8)
-    results = torch.zeros(len(fmts), dtype=torch.float64, device="cuda")
+        values = (rows * cols + cols) if gemv else 2 * n
+        packed_bytes.append(values * _lib.format_info(fid)[1] / 8)
+    results = torch.zeros(len(fmts) * rows, dtype=torch.float64, device="cuda")
     res_ptr = results.data_ptr()
     torch.cuda.synchronize()
 
+    def launch(k, strat, dec=0):
+        x, y = inputs[k]
+        if gemv:
+            ws.gemv(fids[k], layout, accum, x.data_ptr(), y.data_ptr(), rows, cols,
+                    res_ptr + 8 * rows * k, stream, strat, dec)
+        else:
+            ws.dot(fids[k], layout, accum, x.data_ptr(), y.data_ptr(), n, res_ptr + 8 * k,
+                   stream, strat, dec)
+
     def step():
-        for k, fid in enumerate(fids):
-            x, y = inputs[k]
-            ws.dot(fid, layout, accum, x.data_ptr(), y.data_ptr(), n, res_ptr + 8 * k, stream,
-                   strategy)
-        if world > 1:
+        for k in range(len(fids)):
+            launch(k, strategy)
+        if world > 1 and not gemv:
             allreduce_partials(results)
 
     for _ in range(args.warmup):
@@ -344,12 +375,10 @@ def main():
     reps = 20
 
     def time_kernel(k, strat, dec=0):
-        x, y = inputs[k]
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for _ in range(reps):
-            ws.dot(fids[k], layout, accum, x.data_ptr(), y.data_ptr(), n, res_ptr + 8 * k,
-                   stream, strat, dec)
+            launch(k, strat, dec)
         b.record()
         torch.cuda.synchronize()
         return a.elapsed_time(b) / reps
@@ -382,17 +411,16 @@ def main():
 
     # e2e through the C ABI from pinned host buffers
     host_in = [(x.cpu().pin_memory(), y.cpu().pin_memory()) for x, y in inputs]
-    host_out = torch.zeros(len(fmts), dtype=torch.float64).pin_memory()
+    host_out = torch.zeros(len(fmts) * rows, dtype=torch.float64).pin_memory()
     h2d = sum(hx.numel() + hy.numel() for hx, hy in host_in)
 
     def e2e_step():
-        for k, fid in enumerate(fids):
+        for k in range(len(fids)):
             x, y = inputs[k]
             x.copy_(host_in[k][0], non_blocking=True)
             y.copy_(host_in[k][1], non_blocking=True)
-            ws.dot(fid, layout, accum, x.data_ptr(), y.data_ptr(), n, res_ptr + 8 * k, stream,
-                   strategy)
-        if world > 1:
+            launch(k, strategy)
+        if world > 1 and not gemv:
             allreduce_partials(results)
         host_out.copy_(results, non_blocking=True)
 
@@ -421,23 +449,32 @@ def main():
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         threads = host_threads()
         tot_bytes, tot_s, kinds = 0.0, 0.0, set()
+        sample_rows = 16 if gemv else 1
         for k, (name, _) in enumerate(fmts):
             x, y = inputs[k]
             xw = x.cpu().numpy().view(np.uint32)
             yw = y.cpu().numpy().view(np.uint32)
-            stride = 64 if name == "fp64" else _lib.format_info(fids[k])[1]
-            t0 = time.perf_counter()
-            d, s, kind = cpu_reference_dot(name, stride, xw, yw, n, threads)
-            tot_s += time.perf_counter() - t0
-            tot_bytes += packed_bytes[k]
-            kinds.add(kind)
-            ref = np.longdouble(d[0]) + np.longdouble(d[1])
-            sabs = np.longdouble(s[0]) + np.longdouble(s[1])
-            errors[name] = float(abs(np.longdouble(gpu_results[k]) - ref) / sabs) if sabs else 0.0
+            bits = _lib.format_info(fids[k])[1]
+            stride = 64 if name == "fp64" else bits
+            row_words = cols * stride // 32
+            worst = 0.0
+            for r in range(sample_rows):
+                t0 = time.perf_counter()
+                d, s, kind = cpu_reference_dot(name, stride, xw[r * row_words:], yw, cols,
+                                               threads)
+                tot_s += time.perf_counter() - t0
+                tot_bytes += (2 * cols if not gemv else cols + cols / sample_rows) * bits / 8
+                kinds.add(kind)
+                ref = np.longdouble(d[0]) + np.longdouble(d[1])
+                sabs = np.longdouble(s[0]) + np.longdouble(s[1])
+                got = np.longdouble(gpu_results[k * rows + r])
+                worst = max(worst, float(abs(got - ref) / sabs) if sabs else 0.0)
+            errors[name] = worst
+        what = (f"{sample_rows} rows of each of the {len(fmts)} matrices ({cols} columns)"
+                if gemv else f"the full workload ({len(fmts)} DOTs x {n} values)")
         cpu_baseline = {"value": tot_bytes / tot_s / 1e9, "unit": "GB/s", "cores": threads,
                         "kind": "reference" if kinds == {"reference"} else "port",
-                        "sample": f"the full workload ({len(fmts)} DOTs x {n} values), "
-                                  "host decode + compensated long-double DOT"}
+                        "sample": what + ", host decode + compensated long-double DOT"}
 
     clk = clocks.summary()
     line = {
@@ -455,12 +492,13 @@ def main():
                        for f, t, g in per_kernel],
         "strategy": args.strategy,
         "normalized_error": errors or None,
-        "roofline": {"bound": "hbm", "kernel": f"dot_kernel[{dom[0]}]", "achieved": dom[2],
+        "roofline": {"bound": "hbm", "kernel": f"{'gemv' if gemv else 'dot'}_kernel[{dom[0]}]",
+                     "achieved": dom[2],
                      "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
                      "frac": dom[2] / peak, "traffic": traffic},
         "cpu_baseline": cpu_baseline,
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": 8 * len(fmts)},
+                "d2h_bytes_per_step": 8 * len(fmts) * rows},
         "gpu_launches": len(fmts) * args.steps,
         "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"],
                    "reasons": clk["reasons"]},
