@@ -579,11 +579,11 @@ __global__ void __launch_bounds__(kThreads)
 // Geometry of one tile: every thread owns kValuesPerThread consecutive codes
 // in units of UW words (UW = S / gcd(S, 32) is odd, so a warp reading word k
 // of 32 consecutive units hits 32 different banks).
-template <int S> struct tma_shape {
+template <int S, int RING = 64 * 1024, int VPT_ = (S >= 24 ? 16 : 32)> struct tma_shape {
   static constexpr int G = gcd_int(S, 32);
   static constexpr int UW = S / G;                 // words per unit
   static constexpr int UV = S == 64 ? 1 : 32 / G;  // codes per unit
-  static constexpr int VPT = S >= 24 ? 16 : 32;    // codes per thread per tile
+  static constexpr int VPT = VPT_;                 // codes per thread per tile
   static constexpr int V = VPT / UV;               // units per thread per tile
   // Units of one or two words are read four words at a time: one 16-byte
   // shared load per operand, a quarter warp covering 128 contiguous bytes
@@ -595,13 +595,20 @@ template <int S> struct tma_shape {
   static constexpr int TILE_WORDS = kThreads * V * UW;
   static constexpr int TILE_BYTES = TILE_WORDS * 4;  // per vector
   static constexpr uint64_t TILE_VALUES = static_cast<uint64_t>(kThreads) * VPT;
-  static constexpr int RING_BYTES = 64 * 1024;
+  static constexpr int RING_BYTES = RING;
   static constexpr int STAGES_RAW = RING_BYTES / (2 * TILE_BYTES);
   static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
   static_assert(TILE_BYTES % 16 == 0, "bulk copies move 16-byte multiples");
   static_assert(V * UV == VPT, "units tile the thread's codes");
   static_assert(V % GROUP == 0, "loads tile the thread's units");
 };
+
+// Codecs with a shared decode table get a 32 KiB ring, so that more blocks
+// -- more warps to hide the table lookups' latency -- fit an SM beside the
+// table (lns8_r3, FP32: 5116 -> 5432 GB/s; 16-bit codes keep two 32 KiB
+// stages, since halving their tiles cost 5 %).
+template <class Codec>
+using tma_shape_of = tma_shape<Codec::kS, ((Codec::kTableBytes > 0) ? 32 * 1024 : 64 * 1024)>;
 
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 2 GHz
 
@@ -658,7 +665,7 @@ __global__ void __launch_bounds__(kThreads)
     dot_tma_kernel(const dot_params p) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ double scratch[kThreads / 32];
-  using shape = tma_shape<Codec::kS>;
+  using shape = tma_shape_of<Codec>;
   constexpr int UV = shape::UV;
   constexpr int V = shape::V;
   constexpr int GROUP = shape::GROUP;
@@ -777,7 +784,7 @@ kernel_entry make_entry(int strategy, int table_kind) {
   e.stride = Codec::kS;
   e.table_kind = table_kind;
   if (strategy == AUT_STRATEGY_TMA) {
-    using shape = aut::dev::tma_shape<Codec::kS>;
+    using shape = aut::dev::tma_shape_of<Codec>;
     e.fn = aut::dev::dot_tma_kernel<Codec, Acc>;
     e.smem = Codec::kTableBytes + shape::STAGES * 2 * shape::TILE_BYTES;
     e.tile_values = shape::TILE_VALUES;
