@@ -7,12 +7,14 @@
 // writes its B/gcd whole words, so no two threads touch one word.  LNS codes
 // come from a binary search over thresholds computed with the host's log2,
 // which makes them equal to the host encoder's for every input.
+#include "dot_device.cuh"
 #include "internal.hpp"
 
 #include "aut/detail/codec_core.hpp"
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 
 namespace aut::dev {
@@ -223,6 +225,81 @@ __global__ void generate_kernel(int kind, uint64_t seed, int vector_id,
     out[i] = synthetic(kind, seed, vector_id, first + i);
 }
 
+// ---- the generic DOT: any registered format, one value per thread ---------------
+// The runtime switch over the registry (the reference compiles one binary per
+// width, src/bitwidth_strategy_bench.cu:955-1211): codes are read by absolute
+// value index (one or two word loads, consecutive threads on consecutive
+// values, so a warp's loads coalesce) and decoded by the bit-exact decoders
+// above; products go into the same accumulators and single-pass grid
+// reduction as the fused kernels.
+struct generic_dot_params {
+  codec_params codec;
+  const unsigned char *x;
+  const unsigned char *y;
+  uint64_t n;
+  uint64_t x_stride, y_stride;              // bytes between the pairs of a batch
+  uint64_t x_first, y_first;                // value index of pair 0
+  uint64_t x_index_stride, y_index_stride;  // values between the pairs of a batch
+  int table_smem_bytes;  // LNS: full decode table staged in shared memory
+  double *partials;
+  unsigned int *tickets;
+  double *results;
+};
+
+template <class Acc, bool kF32>
+__global__ void __launch_bounds__(kThreads) dot_generic_kernel(const generic_dot_params g) {
+  extern __shared__ __align__(16) unsigned char table[];
+  __shared__ double scratch[kThreads / 32];
+  codec_params c = g.codec;
+  if (g.table_smem_bytes > 0) {
+    const uint4 *src = kF32 ? reinterpret_cast<const uint4 *>(c.lns_f32)
+                            : reinterpret_cast<const uint4 *>(c.lns_f64);
+    uint4 *dst = reinterpret_cast<uint4 *>(table);
+    for (int k = threadIdx.x; k < g.table_smem_bytes / 16; k += kThreads) dst[k] = src[k];
+    __syncthreads();
+    if constexpr (kF32)
+      c.lns_f32 = reinterpret_cast<const float *>(table);
+    else
+      c.lns_f64 = reinterpret_cast<const double *>(table);
+  }
+  const unsigned int batch = blockIdx.y;
+  const unsigned char *xb = g.x + batch * g.x_stride;
+  const unsigned char *yb = g.y + batch * g.y_stride;
+  const uint64_t xo = g.x_first + batch * g.x_index_stride;
+  const uint64_t yo = g.y_first + batch * g.y_index_stride;
+  const uint32_t mask = aut::detail::low_mask32(c.total_bits);
+
+  Acc acc;
+  auto mac = [&](int slot, uint32_t rx, uint32_t ry) {
+    if constexpr (kF32)
+      acc.mac(slot, decode_one_f32(c, rx & mask), decode_one_f32(c, ry & mask));
+    else
+      acc.mac_d(slot, decode_one_f64(c, rx & mask), decode_one_f64(c, ry & mask));
+  };
+  const uint64_t step = static_cast<uint64_t>(gridDim.x) * kThreads;
+  uint64_t i = static_cast<uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  int done = 0;
+  // four independent values in flight per thread
+  for (; i + 3 * step < g.n; i += 4 * step) {
+    uint32_t rx[4], ry[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      rx[k] = load_any(xb, c.stride, xo + i + k * step);
+      ry[k] = load_any(yb, c.stride, yo + i + k * step);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) mac(k, rx[k], ry[k]);
+    if ((done += 4) == 128) {  // 32 products per FP32 chain between FP64 carries
+      acc.flush();
+      done = 0;
+    }
+  }
+  for (; i < g.n; i += step) mac(0, load_any(xb, c.stride, xo + i), load_any(yb, c.stride, yo + i));
+  const double s = block_sum(acc.value(), scratch);
+  grid_finish(s, g.partials + static_cast<uint64_t>(batch) * gridDim.x, g.tickets + batch,
+              g.results + batch, scratch);
+}
+
 } // namespace aut::dev
 
 namespace aut::lib {
@@ -310,6 +387,80 @@ aut_status launch_generate(int32_t kind, uint64_t seed, int32_t vector_id,
   aut::dev::generate_kernel<<<grid_for(n), 256, 0, stream>>>(kind, seed, vector_id,
                                                              first, n, out);
   AUT_CUDA_TRY(cudaGetLastError());
+  return AUT_OK;
+}
+
+bool generic_dot_ok(const format_desc &f, int32_t accum) {
+  switch (f.family) {
+  case AUT_FAMILY_BINARY: {
+    if (accum == AUT_ACCUM_FP64) return true;
+    // FP32 only where every value is an FP32 value (decode_fp32_bits,
+    // decoder_strategy_core.hpp:297-303: E <= 8, M <= 23)
+    const int m = f.total_bits - f.exponent_bits - 1;
+    return f.exponent_bits <= 8 && m <= 23;
+  }
+  case AUT_FAMILY_FP64_PREFIX: return accum == AUT_ACCUM_FP64;
+  case AUT_FAMILY_LNS: return f.total_bits <= 16;  // host-built decode tables
+  default: return false;  // raw FP32 / FP64 have fused kernels
+  }
+}
+
+aut_status generic_dot_launch(aut_workspace *ws, const format_desc &f, int32_t format,
+                              int32_t layout, int32_t accum, const void *x, const void *y,
+                              uint64_t n, uint32_t batch, const batch_layout &bl,
+                              double *results, cudaStream_t stream, double *partials,
+                              unsigned int *tickets, int max_blocks_total) {
+  if (!generic_dot_ok(f, accum))
+    return fail(AUT_ERR_UNSUPPORTED, std::string("no DOT kernel for ") + f.name +
+                                         " with this accumulator");
+  aut::dev::generic_dot_params g{};
+  aut_status st = make_params(ws, f, format, layout, g.codec);
+  if (st != AUT_OK) return st;
+  const bool f32 = accum == AUT_ACCUM_FP32;
+  if (f.family == AUT_FAMILY_LNS) {
+    const int bytes = (1 << f.total_bits) * (f32 ? 4 : 8);
+    g.table_smem_bytes = bytes <= 32 * 1024 ? bytes : 0;  // larger tables stay in L2
+  }
+  using fn_t = void (*)(aut::dev::generic_dot_params);
+  const fn_t fn = f32 ? aut::dev::dot_generic_kernel<aut::dev::acc_f32, true>
+                      : aut::dev::dot_generic_kernel<aut::dev::acc_f64, false>;
+  static std::atomic<int> occupancy[2];  // blocks per SM without a staged table
+  int per_sm = occupancy[f32].load(std::memory_order_relaxed);
+  if (g.table_smem_bytes > 0 || per_sm == 0) {
+    AUT_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      32 * 1024));
+    AUT_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+        &per_sm, fn, aut::dev::kThreads, g.table_smem_bytes));
+    if (g.table_smem_bytes == 0) occupancy[f32].store(per_sm, std::memory_order_relaxed);
+  }
+  if (per_sm < 1) per_sm = 1;
+  const uint64_t cap = static_cast<uint64_t>(ws->sm_count) * per_sm;
+  uint64_t wanted = (n + aut::dev::kThreads * 16 - 1) / (aut::dev::kThreads * 16);
+  if (wanted == 0) wanted = 1;
+  for (uint32_t b0 = 0; b0 < batch; b0 += kMaxBatchPerLaunch) {
+    const uint32_t nb = batch - b0 < static_cast<uint32_t>(kMaxBatchPerLaunch)
+                            ? batch - b0
+                            : static_cast<uint32_t>(kMaxBatchPerLaunch);
+    uint64_t per_pair = (cap + nb - 1) / nb;
+    if (per_pair > wanted) per_pair = wanted;
+    if (per_pair > static_cast<uint64_t>(max_blocks_total)) per_pair = max_blocks_total;
+    if (per_pair < 1) per_pair = 1;
+    g.x = static_cast<const unsigned char *>(x) + static_cast<uint64_t>(b0) * bl.x_stride;
+    g.y = static_cast<const unsigned char *>(y) + static_cast<uint64_t>(b0) * bl.y_stride;
+    g.n = n;
+    g.x_stride = bl.x_stride;
+    g.y_stride = bl.y_stride;
+    g.x_first = static_cast<uint64_t>(b0) * bl.x_index_stride;
+    g.y_first = static_cast<uint64_t>(b0) * bl.y_index_stride;
+    g.x_index_stride = bl.x_index_stride;
+    g.y_index_stride = bl.y_index_stride;
+    g.partials = partials;
+    g.tickets = tickets;
+    g.results = results + b0;
+    dim3 grid(static_cast<unsigned>(per_pair), nb);
+    fn<<<grid, aut::dev::kThreads, g.table_smem_bytes, stream>>>(g);
+    AUT_CUDA_TRY(cudaGetLastError());
+  }
   return AUT_OK;
 }
 

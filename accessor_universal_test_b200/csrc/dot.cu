@@ -926,10 +926,27 @@ aut_status blocks_per_sm(kernel_entry &e) {
 
 } // namespace
 
+aut_status generic_dot_launch(aut_workspace *ws, const format_desc &f, int32_t format,
+                              int32_t layout, int32_t accum, const void *x, const void *y,
+                              uint64_t n, uint32_t batch, const batch_layout &bl,
+                              double *results, cudaStream_t stream, double *partials,
+                              unsigned int *tickets, int max_blocks_total);
+
+// Formats with fused kernels (ids 0..10) never fall back to the generic DOT;
+// every other registered format runs it when it decodes exactly.
+static bool has_fused_kernel(int32_t format, int32_t layout, int32_t accum) {
+  return lookup(format, layout, accum, AUT_STRATEGY_AUTO).fn != nullptr;
+}
+
+static bool generic_format(int32_t format) {
+  return format > AUT_FMT_LNS16_R11 && find_format(format) != nullptr;
+}
+
 int32_t dot_supported(int32_t format, int32_t layout, int32_t accum) {
   if (layout != AUT_LAYOUT_DENSE && layout != AUT_LAYOUT_PADDED) return 0;
   if (accum != AUT_ACCUM_FP32 && accum != AUT_ACCUM_FP64) return 0;
-  return lookup(format, layout, accum, AUT_STRATEGY_AUTO).fn != nullptr ? 1 : 0;
+  if (has_fused_kernel(format, layout, accum)) return 1;
+  return generic_format(format) && generic_dot_ok(*find_format(format), accum) ? 1 : 0;
 }
 
 // The vector paths need 16-byte aligned streams for every pair of the batch.
@@ -967,6 +984,20 @@ aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
   // SCALAR runs the LDG kernel with the vector path switched off, so every
   // code goes through the per-value load and decode.
   const bool scalar_only = strategy == AUT_STRATEGY_SCALAR;
+  if (generic_format(format)) {
+    // the generic DOT reads one value per thread: strategy AUTO or SCALAR,
+    // decoder AUTO, DIRECT (bit formats) or FULL_LUT (LNS: host-built table)
+    const format_desc &f = *find_format(format);
+    const int direct = f.family == AUT_FAMILY_LNS ? AUT_DECODER_FULL_LUT : AUT_DECODER_DIRECT;
+    if ((strategy != AUT_STRATEGY_AUTO && !scalar_only) ||
+        (decoder != AUT_DECODER_AUTO && decoder != direct))
+      return fail(AUT_ERR_UNSUPPORTED,
+                  "formats without fused kernels take strategy AUTO/SCALAR and their "
+                  "direct (or full-table) decoder");
+    return generic_dot_launch(ws, f, format, layout, accum, x, y, n, batch, bl, results,
+                              static_cast<cudaStream_t>(stream), partials, tickets,
+                              max_blocks_total);
+  }
   kernel_entry e = lookup(format, layout, accum,
                           scalar_only ? AUT_STRATEGY_LDG : strategy, decoder);
   if (e.fn == nullptr)
@@ -980,6 +1011,10 @@ aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
     const lns_tables *t = nullptr;
     st = lns_tables_for(ws, format, &t);
     if (st != AUT_OK) return st;
+    if ((e.table_kind == 3 && !t->split_f32) || (e.table_kind == 4 && !t->split_f64))
+      return fail(AUT_ERR_UNSUPPORTED,
+                  "this host's exp2/exp2f break the split LNS decode identity that the "
+                  "fraction-table kernels rely on");
     table = e.table_kind == 1   ? static_cast<const void *>(t->full_f32)
             : e.table_kind == 2 ? static_cast<const void *>(t->full_f64)
             : e.table_kind == 3 ? static_cast<const void *>(t->frac_f32)

@@ -47,7 +47,15 @@ struct lns_tables {
   double *frac_f64 = nullptr;  // 2^R entries: exp2(f / 2^R)
   double *thresholds = nullptr; // encode thresholds, 2^(B-1) - 2 entries
   double zero_threshold = 0.0; // smallest magnitude that does not encode to 0
+  // +-2^q * frac[f] equals the full decode for every code (FP32 / FP64), so
+  // the fraction-table kernels may serve this format on this host
+  int split_f32 = 0;
+  int split_f64 = 0;
 };
+
+// The generic DOT (one value per thread, any registered format): whether it
+// decodes `f` exactly for accumulator `accum`, and its launcher (codec.cu).
+bool generic_dot_ok(const format_desc &f, int32_t accum);
 
 constexpr int kMaxBatchPerLaunch = 1024;
 
@@ -60,7 +68,7 @@ struct batch_layout {
   uint64_t x_stride = 0, y_stride = 0;
   uint64_t x_index_stride = 0, y_index_stride = 0;
 };
-constexpr int kLnsFormatsCached = 8;
+constexpr int kLnsFormatsCached = 24;  // every registered LNS format
 
 } // namespace aut::lib
 
@@ -72,7 +80,10 @@ struct aut_workspace {
   unsigned int *tickets = nullptr; // [kMaxBatchPerLaunch + 1], kept at zero;
                                    // the last word is the sticky status
   std::mutex mutex;
-  int lns_ids[aut::lib::kLnsFormatsCached] = {-1, -1, -1, -1, -1, -1, -1, -1};
+  int lns_ids[aut::lib::kLnsFormatsCached];
+  aut_workspace() {
+    for (int &id : lns_ids) id = -1;
+  }
   aut::lib::lns_tables lns[aut::lib::kLnsFormatsCached];
 };
 

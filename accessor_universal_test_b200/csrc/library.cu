@@ -252,8 +252,10 @@ aut_status build_lns_tables(const format_desc &f, lns_tables &t) {
     frac32[k] = ::exp2f(static_cast<float>(k) / static_cast<float>(frac));
     frac64[k] = std::exp2(static_cast<double>(k) / static_cast<double>(frac));
   }
-  // The fraction-table kernels decode +-2^q * T[f] with an exponent add; check
-  // that this host's libm makes that identical to the full decode.
+  // The fraction-table kernels decode +-2^q * T[f] with an exponent add;
+  // record whether this host's libm makes that identical to the full decode
+  // (the full-table kernels serve the format either way).
+  t.split_f32 = t.split_f64 = 1;
   for (size_t r = 0; r < full; ++r) {
     const uint32_t raw = static_cast<uint32_t>(r);
     if ((raw & aut::detail::lns_log_mask(Bb)) == aut::detail::lns_special(Bb)) continue;
@@ -263,9 +265,8 @@ aut_status build_lns_tables(const format_desc &f, lns_tables &t) {
     const float s32 = std::ldexp(frac32[fi], q);
     const double s64 = std::ldexp(frac64[fi], q);
     const bool neg = (raw & aut::detail::lns_sign_mask(Bb)) != 0;
-    if ((neg ? -s32 : s32) != full32[r] || (neg ? -s64 : s64) != full64[r])
-      return fail(AUT_ERR_UNSUPPORTED,
-                  "host exp2/exp2f break the split LNS decode identity");
+    if ((neg ? -s32 : s32) != full32[r]) t.split_f32 = 0;
+    if ((neg ? -s64 : s64) != full64[r]) t.split_f64 = 0;
   }
   // Encode thresholds: thr[j] = smallest magnitude with log code > min + j.
   const int64_t lo = -static_cast<int64_t>(aut::detail::lns_special(Bb)) + 1;

@@ -1,0 +1,99 @@
+"""The generic DOT (every registered format without a fused kernel) against
+the oracle: the runtime switch over the reference's format registries
+(src/bitwidth_strategy_bench.cu:955-1211, lns_benchmark_core.hpp:44-61)."""
+import numpy as np
+import pytest
+
+from gpu_util import SEED, TOL, normalized_error
+
+pytestmark = pytest.mark.gpu
+
+FUSED = {"fp32", "fp64", "e2m3", "e8m0", "e8m1", "e8m3", "e8m5", "bf16_e8m7", "e8m15",
+         "lns8_r3", "lns16_r11"}
+
+
+def _generic_formats():
+    from accessor_universal_test_b200 import _lib
+    lib = _lib.load()
+    names = []
+    for fid in range(lib.aut_format_count()):
+        name = lib.aut_format_name(fid).decode()
+        if name not in FUSED:
+            names.append(name)
+    return names
+
+
+def _pair(ws, orc, name, layout, n, seed=SEED):
+    import torch
+    from accessor_universal_test_b200 import _lib
+    fid = _lib.format_id(name)
+    desc = _lib.format_info(fid)
+    kind = 3 if desc[0] == _lib.FAMILY_LNS else 0
+    codes = [orc.encode(desc, orc.synthetic(kind, seed, v, n)) for v in (0, 1)]
+    bufs = []
+    for c in codes:
+        b = np.zeros(_lib.storage_bytes(fid, layout, n), np.uint8)
+        _lib.check(_lib.load().aut_pack_host(fid, layout, c.ctypes.data, n, b.ctypes.data))
+        bufs.append(torch.from_numpy(b).cuda())
+    return fid, desc, codes, bufs
+
+
+def test_every_registered_format_has_a_dot(autlib):
+    from accessor_universal_test_b200 import _lib
+    names = _generic_formats()
+    assert len(names) == autlib.aut_format_count() - len(FUSED)
+    for name in names:
+        fid = _lib.format_id(name)
+        fam, bits, _, _ = _lib.format_info(fid)
+        want64 = 0 if (fam == _lib.FAMILY_LNS and bits > 16) else 1
+        assert autlib.aut_dot_supported(fid, 0, 1) == want64, name
+
+
+@pytest.mark.parametrize("layout", [0, 1])
+def test_generic_dot_matches_oracle_on_every_format(ws, orc, autlib, layout):
+    import torch
+    from accessor_universal_test_b200 import _lib
+    checked = 0
+    for name in _generic_formats():
+        fid = _lib.format_id(name)
+        for n in (1, 4099, 65536 + 13):
+            accs = [a for a in (0, 1) if autlib.aut_dot_supported(fid, layout, a)]
+            if not accs:
+                continue
+            _, desc, codes, (x, y) = _pair(ws, orc, name, layout, n)
+            (d, s) = orc.dot_codes(desc, codes[0], codes[1], threads=4)
+            ref = np.longdouble(d[0]) + np.longdouble(d[1])
+            sabs = np.longdouble(s[0]) + np.longdouble(s[1])
+            for acc in accs:
+                res = torch.full((1,), float("nan"), dtype=torch.float64, device="cuda")
+                ws.dot(fid, layout, acc, x.data_ptr(), y.data_ptr(), n, res.data_ptr())
+                torch.cuda.synchronize()
+                got = res.item()
+                if not np.isfinite(float(ref)):
+                    assert np.isnan(got) or got == float(ref), (name, n, acc, got)
+                    continue
+                err = normalized_error(got, ref, sabs)
+                assert err <= TOL[acc], (name, layout, n, acc, got, float(ref), float(err))
+                checked += 1
+    assert checked > 300
+
+
+@pytest.mark.parametrize("name", ["e3m4", "e5m11", "e11m20", "lns16_r4", "lns6_r2", "e0m31"])
+def test_generic_gemv_and_batched(ws, orc, name):
+    """Rows of a generic-format matrix, 16-byte aligned or not, and batches."""
+    import torch
+    from accessor_universal_test_b200 import _lib
+    fid = _lib.format_id(name)
+    desc = _lib.format_info(fid)
+    for rows, cols in ((40, 2048), (33, 999)):
+        _, _, mcodes, (m, _) = _pair(ws, orc, name, 0, rows * cols)
+        _, _, vcodes, (v, _) = _pair(ws, orc, name, 0, cols, seed=SEED + 1)
+        out = torch.full((rows,), float("nan"), dtype=torch.float64, device="cuda")
+        ws.gemv(fid, 0, 1, m.data_ptr(), v.data_ptr(), rows, cols, out.data_ptr())
+        torch.cuda.synchronize()
+        got = out.cpu().numpy()
+        for r in range(rows):
+            d, s = orc.dot_codes(desc, mcodes[0][r * cols:(r + 1) * cols], vcodes[0], threads=1)
+            ref = np.longdouble(d[0]) + np.longdouble(d[1])
+            sabs = np.longdouble(s[0]) + np.longdouble(s[1])
+            assert normalized_error(got[r], ref, sabs) <= TOL[1], (name, rows, cols, r)

@@ -71,7 +71,16 @@ def test_dot_support_matrix(autlib):
             assert autlib.aut_dot_supported(f, layout, _lib.ACC_FP64) == 1, name
             want = 0 if name == "fp64" else 1
             assert autlib.aut_dot_supported(f, layout, _lib.ACC_FP32) == want, name
-    assert autlib.aut_dot_supported(_lib.format_id("e3m4"), _lib.DENSE, _lib.ACC_FP32) == 0
+    # the generic DOT: FP32 where every value is an FP32 value (E <= 8,
+    # M <= 23), FP64 for every bit format, LNS up to 16 bits
+    expect = {("e3m4", 0): 1, ("e3m4", 1): 1, ("e9m22", 0): 0, ("e9m22", 1): 1,
+              ("e0m31", 0): 0, ("e0m31", 1): 1, ("e0m23", 0): 1, ("e1m14", 0): 1,
+              ("e11m4", 0): 0, ("e11m4", 1): 1, ("lns16_r4", 0): 1, ("lns16_r4", 1): 1,
+              ("lns32_r20", 0): 0, ("lns32_r20", 1): 0}
+    for (name, acc), want in expect.items():
+        for layout in (_lib.DENSE, _lib.PADDED):
+            got = autlib.aut_dot_supported(_lib.format_id(name), layout, acc)
+            assert got == want, (name, acc, layout)
     assert autlib.aut_dot_supported(0, 7, 0) == 0
 
 
