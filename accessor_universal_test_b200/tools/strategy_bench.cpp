@@ -166,6 +166,20 @@ struct decoder_choice {
 
 std::vector<decoder_choice> decoders_for(const std::string &fmt, int32_t accum) {
   const int t = accum == AUT_ACCUM_FP64 ? 8 : 4;
+  static const std::set<std::string> fused = {"fp32", "fp64", "e2m3", "e8m0", "e8m1",
+                                              "e8m3", "e8m5", "bf16_e8m7", "e8m15",
+                                              "lns8_r3", "lns16_r11"};
+  if (!fused.count(fmt)) {  // the generic DOT (runtime format switch)
+    const int32_t fid = aut_format_id(fmt.c_str());
+    int32_t family = 0, bits = 0, e = 0, fin = 0;
+    aut_format_info(fid, &family, &bits, &e, &fin);
+    if (family == AUT_FAMILY_LNS) {
+      const int bytes = (1 << bits) * t;
+      return {{AUT_DECODER_AUTO, bytes <= 32 * 1024 ? "full_lut_shared" : "full_lut_global",
+               "ordinary", bytes}};
+    }
+    return {{AUT_DECODER_AUTO, "generic", "ordinary", 0}};
+  }
   if (fmt == "lns8_r3") return {{AUT_DECODER_FULL_LUT, "full_lut_shared", "ordinary", 256 * 32 * t}};
   if (fmt == "lns16_r11") {
     std::vector<decoder_choice> d;
@@ -341,6 +355,15 @@ int main(int argc, char **argv) {
                 if (!o.variants.empty() && !o.variants.count(id.str()) &&
                     !o.variants.count(qualified))
                   continue;
+                // formats without fused kernels take the per-value access only
+                {
+                  device_buffer probe(64);
+                  const aut_status st = aut_dot_variant(ws, fid, layout, accum, ac.strategy,
+                                                        dc.id, probe.p, probe.p, 0, d_result,
+                                                        nullptr);
+                  if (st == AUT_ERR_UNSUPPORTED) continue;
+                  aut_check(st, "aut_dot_variant");
+                }
                 for (int power : o.dot_powers) {
                   const uint64_t n = uint64_t{1} << power;
                   device_buffer xs(aut_storage_bytes(fid, layout, n));
