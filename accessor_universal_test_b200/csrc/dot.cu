@@ -26,6 +26,17 @@
 
 namespace aut::dev {
 
+// Decode parameters of a format without a dedicated codec (rt_codec below).
+struct rt_params {
+  uint32_t bits;          // B: code width (padded containers: the code's own width)
+  uint32_t exponent;      // E (0: fixed point)
+  uint32_t special_from;  // top-aligned magnitudes >= this are inf/NaN to build (0: none)
+  uint32_t pad;
+  float scale32;          // 2^(127 - bias) (fixed point: 2^126)
+  uint32_t pad2;
+  double scale64;         // 2^(1023 - bias) (fixed point: 2^1022)
+};
+
 struct dot_params {
   const unsigned char *x;
   const unsigned char *y;
@@ -42,6 +53,7 @@ struct dot_params {
   unsigned int *tickets;  // [gridDim.y]
   double *results;        // [gridDim.y]
   unsigned int *status;   // sticky error bits (AUT_STATUS_*)
+  rt_params rt;           // rt_codec only
 };
 
 // ---------------------------------------------------------------------------
@@ -60,7 +72,7 @@ template <int S, int W> struct e8_codec {
   static constexpr int kU = packet_shape<S>::Q == 1 ? 4 : (S == 24 ? 2 : 1);
   static constexpr int kTableBytes = 0;
   static constexpr bool kExactLanes = false;
-  __device__ static void prepare(const void *, unsigned char *) {}
+  __device__ static void prepare(const dot_params &, unsigned char *) {}
 
   template <int NV, class Acc>
   __device__ __forceinline__ static void values(const uint32_t *xw,
@@ -91,7 +103,7 @@ struct f64_codec {
   static constexpr int kU = 4;
   static constexpr int kTableBytes = 0;
   static constexpr bool kExactLanes = false;
-  __device__ static void prepare(const void *, unsigned char *) {}
+  __device__ static void prepare(const dot_params &, unsigned char *) {}
 
   template <int NV, class Acc>
   __device__ __forceinline__ static void values(const uint32_t *xw,
@@ -130,7 +142,7 @@ template <int S> struct e2m3_codec {
   static constexpr int kU = S == 8 ? 4 : 1;
   static constexpr int kTableBytes = 0;
   static constexpr bool kExactLanes = true;
-  __device__ static void prepare(const void *, unsigned char *) {}
+  __device__ static void prepare(const dot_params &, unsigned char *) {}
 
   // Codes 4g .. 4g+3 of the word array, one per byte (low 6 bits).
   __device__ __forceinline__ static uint32_t bytes4(const uint32_t *w, int g) {
@@ -201,7 +213,8 @@ template <typename T> struct lns8_codec {
   static constexpr int kU = 4;
   static constexpr int kTableBytes = 256 * 32 * static_cast<int>(sizeof(T));
   static constexpr bool kExactLanes = false;
-  __device__ static void prepare(const void *table, unsigned char *smem) {
+  __device__ static void prepare(const dot_params &p, unsigned char *smem) {
+    const void *table = p.table;
     const T *g = static_cast<const T *>(table);
     T *s = reinterpret_cast<T *>(smem);
     for (int e = threadIdx.x; e < 256 * 32; e += kThreads) s[e] = g[e >> 5];
@@ -253,7 +266,8 @@ template <typename T> struct lns16_codec {
   static constexpr int kU = 4;
   static constexpr int kTableBytes = 2048 * static_cast<int>(sizeof(T));
   static constexpr bool kExactLanes = false;
-  __device__ static void prepare(const void *table, unsigned char *smem) {
+  __device__ static void prepare(const dot_params &p, unsigned char *smem) {
+    const void *table = p.table;
     const T *g = static_cast<const T *>(table);
     T *s = reinterpret_cast<T *>(smem);
     for (int e = threadIdx.x; e < 2048; e += kThreads) s[e] = g[e];
@@ -319,7 +333,8 @@ struct lns16_full_codec {
   static constexpr int kU = 4;
   static constexpr int kTableBytes = 32768 * 4;
   static constexpr bool kExactLanes = false;
-  __device__ static void prepare(const void *table, unsigned char *smem) {
+  __device__ static void prepare(const dot_params &p, unsigned char *smem) {
+    const void *table = p.table;
     const uint4 *g = static_cast<const uint4 *>(table);
     uint4 *s = reinterpret_cast<uint4 *>(smem);
     for (int e = threadIdx.x; e < 32768 / 4; e += kThreads) s[e] = g[e];
@@ -390,7 +405,8 @@ template <typename T> struct lns16_fused_codec {
   static constexpr int kTableBytes = 2048 * static_cast<int>(sizeof(T));
   static constexpr bool kExactLanes = false;
   static constexpr int kMant = sizeof(T) == 4 ? 23 : 20;  // exponent shift in the top word
-  __device__ static void prepare(const void *table, unsigned char *smem) {
+  __device__ static void prepare(const dot_params &p, unsigned char *smem) {
+    const void *table = p.table;
     const T *g = static_cast<const T *>(table);
     T *s = reinterpret_cast<T *>(smem);
     for (int e = threadIdx.x; e < 2048; e += kThreads) {
@@ -498,6 +514,84 @@ template <typename T> struct lns16_fused_codec {
   }
 };
 
+// The rest of the registry's bit formats (IEEE-like E/M of any width, E0
+// fixed point, FP64 prefixes), decoded by runtime parameters: the code is
+// moved to the top of a word (sign at bit 31), its magnitude shifted right
+// so that its exponent field lands on the target's exponent field, and one
+// multiply by 2^(target bias - format bias) rebiases it -- the half-to-float
+// conversion, exact for normals and, through the hardware's denormal
+// arithmetic, for subnormals (decode_words_masked,
+// decoder_strategy_core.hpp:226-262, computes the same values with integer
+// steps).  Formats with inf/NaN whose exponent is narrower than the target's
+// build those explicitly.  S is the slot width (dense: the code width B;
+// padded: the container, the code in its low B bits).
+template <int S, typename T, bool kDense> struct rt_codec {
+  static constexpr int kS = S;
+  static constexpr int kU = 1;
+  static constexpr int kTableBytes = static_cast<int>(sizeof(rt_params));
+  static constexpr bool kExactLanes = false;
+  __device__ static void prepare(const dot_params &p, unsigned char *smem) {
+    if (threadIdx.x == 0) *reinterpret_cast<rt_params *>(smem) = p.rt;
+  }
+
+  // t: the code at bits [32 - B, 32); e: E; from: first inf/NaN magnitude
+  __device__ __forceinline__ static float dec32(uint32_t t, uint32_t e, uint32_t from,
+                                                float scale) {
+    const uint32_t mag = t & 0x7fffffffu;
+    uint32_t bits = (mag >> (8u - e)) | (t & 0x80000000u);
+    if (from != 0u && mag >= from)
+      bits = (t & 0x80000000u) | 0x7f800000u | ((t << (e + 1u)) >> 9);
+    return __uint_as_float(bits) * scale;
+  }
+  __device__ __forceinline__ static double dec64(uint32_t t, uint32_t e, uint32_t from,
+                                                 double scale) {
+    const uint64_t sign = static_cast<uint64_t>(t & 0x80000000u) << 32;
+    const uint64_t mag = static_cast<uint64_t>(t & 0x7fffffffu) << 32;
+    uint64_t bits = (mag >> (11u - e)) | sign;
+    if (from != 0u && (t & 0x7fffffffu) >= from)
+      bits = sign | 0x7ff0000000000000ull | ((static_cast<uint64_t>(t << (e + 1u)) << 32) >> 12);
+    return __longlong_as_double(static_cast<long long>(bits)) * scale;
+  }
+
+  __device__ __forceinline__ static uint32_t top(const uint32_t *w, int v, uint32_t shift) {
+    if constexpr (kDense)
+      return field_top<S, S>(w, v);
+    else
+      return field_low<S, S>(w, v) << shift;
+  }
+
+  template <int NV, class Acc>
+  __device__ __forceinline__ static void values(const uint32_t *xw,
+                                                const uint32_t *yw, Acc &acc,
+                                                float *, const unsigned char *smem) {
+    const rt_params &r = *reinterpret_cast<const rt_params *>(smem);
+    const uint32_t shift = 32u - r.bits, e = r.exponent, from = r.special_from;
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const uint32_t tx = top(xw, v, shift), ty = top(yw, v, shift);
+      if constexpr (sizeof(T) == 4)
+        acc.mac(v, dec32(tx, e, from, r.scale32), dec32(ty, e, from, r.scale32));
+      else
+        acc.mac_d(v, dec64(tx, e, from, r.scale64), dec64(ty, e, from, r.scale64));
+    }
+  }
+
+  template <class Acc>
+  __device__ __forceinline__ static void scalar(const unsigned char *xb, uint64_t i,
+                                                const unsigned char *yb, uint64_t j,
+                                                Acc &acc, const unsigned char *smem) {
+    const rt_params &r = *reinterpret_cast<const rt_params *>(smem);
+    const uint32_t shift = 32u - r.bits;
+    const uint32_t tx = load_code<S, S>(xb, i) << shift, ty = load_code<S, S>(yb, j) << shift;
+    if constexpr (sizeof(T) == 4)
+      acc.mac_d(0, static_cast<double>(dec32(tx, r.exponent, r.special_from, r.scale32)),
+                static_cast<double>(dec32(ty, r.exponent, r.special_from, r.scale32)));
+    else
+      acc.mac_d(0, dec64(tx, r.exponent, r.special_from, r.scale64),
+                dec64(ty, r.exponent, r.special_from, r.scale64));
+  }
+};
+
 template <class Codec, class Acc>
 __device__ __forceinline__ void flush_tile(Acc &acc, float *lanes) {
   if constexpr (Codec::kExactLanes) {
@@ -539,7 +633,7 @@ __global__ void __launch_bounds__(kThreads)
   const uint64_t yo = p.y_first + batch * p.y_index_stride;
 
   if constexpr (Codec::kTableBytes > 0) {
-    Codec::prepare(p.table, smem);
+    Codec::prepare(p, smem);
     __syncthreads();
   }
 
@@ -579,7 +673,8 @@ __global__ void __launch_bounds__(kThreads)
 // Geometry of one tile: every thread owns kValuesPerThread consecutive codes
 // in units of UW words (UW = S / gcd(S, 32) is odd, so a warp reading word k
 // of 32 consecutive units hits 32 different banks).
-template <int S, int RING = 64 * 1024, int VPT_ = (S >= 24 ? 16 : 32)> struct tma_shape {
+template <int S, int RING = 64 * 1024, int VPT_ = (S >= 24 ? 16 : (S <= 4 ? 128 : 32))>
+struct tma_shape {
   static constexpr int G = gcd_int(S, 32);
   static constexpr int UW = S / G;                 // words per unit
   static constexpr int UV = S == 64 ? 1 : 32 / G;  // codes per unit
@@ -590,7 +685,8 @@ template <int S, int RING = 64 * 1024, int VPT_ = (S >= 24 ? 16 : 32)> struct tm
   // (no bank conflicts), and one decode call per four words.  Longer units
   // have an odd word count and are read word by word, one unit per lane,
   // which is conflict-free too.
-  static constexpr int GROUP = UW <= 2 ? 4 / UW : 1;  // units per load
+  static constexpr int GROUP_RAW = UW <= 2 ? 4 / UW : 1;
+  static constexpr int GROUP = GROUP_RAW < V ? GROUP_RAW : V;  // units per load
   static constexpr int LW = UW * GROUP;              // words per load
   static constexpr int TILE_WORDS = kThreads * V * UW;
   static constexpr int TILE_BYTES = TILE_WORDS * 4;  // per vector
@@ -608,7 +704,7 @@ template <int S, int RING = 64 * 1024, int VPT_ = (S >= 24 ? 16 : 32)> struct tm
 // table (lns8_r3, FP32: 5116 -> 5432 GB/s; 16-bit codes keep two 32 KiB
 // stages, since halving their tiles cost 5 %).
 template <class Codec>
-using tma_shape_of = tma_shape<Codec::kS, ((Codec::kTableBytes > 0) ? 32 * 1024 : 64 * 1024)>;
+using tma_shape_of = tma_shape<Codec::kS, ((Codec::kTableBytes > 1024) ? 32 * 1024 : 64 * 1024)>;
 
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 2 GHz
 
@@ -698,7 +794,7 @@ __global__ void __launch_bounds__(kThreads)
     for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1);
     mbar_fence_init();
   }
-  if constexpr (Codec::kTableBytes > 0) Codec::prepare(p.table, smem);
+  if constexpr (Codec::kTableBytes > 0) Codec::prepare(p, smem);
   __syncthreads();
   if (threadIdx.x == 0)
     for (uint64_t k = 0; k < mine && k < STAGES; ++k) issue(k);
@@ -776,6 +872,7 @@ struct kernel_entry {
   int table_kind = 0;   // 0 none, 1 lns full f32, 2 lns full f64, 3 frac f32, 4 frac f64
   uint64_t tile_values = 0;  // codes per block-tile of the vector path
   int blocks_per_sm = 0;
+  int runtime = 0;      // rt_codec: dot_params::rt carries the format
 };
 
 template <class Codec, class Acc>
@@ -795,6 +892,80 @@ kernel_entry make_entry(int strategy, int table_kind) {
                     aut::dev::kThreads * Codec::kU;
   }
   return e;
+}
+
+// TMA-only entry (rt_codec: packets of up to 17 vectors would not fit an
+// LDG thread's registers).
+template <class Codec, class Acc>
+kernel_entry make_tma_entry() {
+  using shape = aut::dev::tma_shape_of<Codec>;
+  kernel_entry e;
+  e.stride = Codec::kS;
+  e.fn = aut::dev::dot_tma_kernel<Codec, Acc>;
+  e.smem = Codec::kTableBytes + shape::STAGES * 2 * shape::TILE_BYTES;
+  e.tile_values = shape::TILE_VALUES;
+  e.runtime = 1;
+  return e;
+}
+
+template <int S, bool kDense>
+kernel_entry rt_entry(int32_t accum) {
+  using namespace aut::dev;
+  return accum == AUT_ACCUM_FP32 ? make_tma_entry<rt_codec<S, float, kDense>, acc_f32>()
+                                 : make_tma_entry<rt_codec<S, double, kDense>, acc_f64>();
+}
+
+// Bit formats without a dedicated codec: the rt_codec TMA kernel of their
+// slot width (the registry's widths; padded containers of 8, 16, 32 bits).
+kernel_entry rt_lookup(int32_t format, int32_t layout, int32_t accum) {
+  const format_desc *f = find_format(format);
+  if (f == nullptr || !generic_dot_ok(*f, accum)) return {};
+  if (f->family != AUT_FAMILY_BINARY && f->family != AUT_FAMILY_FP64_PREFIX) return {};
+  if (layout == AUT_LAYOUT_PADDED) {
+    switch (container_bits(*f)) {
+    case 8: return rt_entry<8, false>(accum);
+    case 16: return rt_entry<16, false>(accum);
+    case 32: return rt_entry<32, false>(accum);
+    default: return {};
+    }
+  }
+  switch (f->total_bits) {
+  case 2: return rt_entry<2, true>(accum);
+  case 3: return rt_entry<3, true>(accum);
+  case 4: return rt_entry<4, true>(accum);
+  case 5: return rt_entry<5, true>(accum);
+  case 6: return rt_entry<6, true>(accum);
+  case 7: return rt_entry<7, true>(accum);
+  case 8: return rt_entry<8, true>(accum);
+  case 9: return rt_entry<9, true>(accum);
+  case 10: return rt_entry<10, true>(accum);
+  case 12: return rt_entry<12, true>(accum);
+  case 14: return rt_entry<14, true>(accum);
+  case 16: return rt_entry<16, true>(accum);
+  case 17: return rt_entry<17, true>(accum);
+  case 20: return rt_entry<20, true>(accum);
+  case 24: return rt_entry<24, true>(accum);
+  case 28: return rt_entry<28, true>(accum);
+  case 32: return rt_entry<32, true>(accum);
+  default: return {};
+  }
+}
+
+// Runtime decode parameters of a bit format for rt_codec.
+aut::dev::rt_params rt_params_for(const format_desc &f, int32_t accum) {
+  aut::dev::rt_params r{};
+  const int E = f.family == AUT_FAMILY_FP64_PREFIX ? 11 : f.exponent_bits;
+  const bool finite = f.family == AUT_FAMILY_BINARY && f.finite != 0;
+  const int bias = E == 0 ? 1 : (1 << (E - 1)) - 1;  // fixed point: value = m 2^-M
+  r.bits = static_cast<uint32_t>(f.total_bits);
+  r.exponent = static_cast<uint32_t>(E);
+  const int target_e = accum == AUT_ACCUM_FP32 ? 8 : 11;
+  r.special_from = (!finite && E > 0 && E < target_e)
+                       ? ((1u << E) - 1u) << (31 - E)
+                       : 0u;
+  r.scale32 = std::ldexp(1.0f, 127 - bias);
+  r.scale64 = std::ldexp(1.0, 1023 - bias);
+  return r;
 }
 
 template <class Codec>
@@ -837,6 +1008,11 @@ int auto_strategy(int32_t format, int32_t layout, int32_t accum) {
 kernel_entry lookup(int32_t format, int32_t layout, int32_t accum, int strategy,
                     int decoder = AUT_DECODER_AUTO) {
   using namespace aut::dev;
+  if (format > AUT_FMT_LNS16_R11) {
+    if (strategy != AUT_STRATEGY_AUTO && strategy != AUT_STRATEGY_TMA) return {};
+    if (decoder != AUT_DECODER_AUTO && decoder != AUT_DECODER_DIRECT) return {};
+    return rt_lookup(format, layout, accum);
+  }
   if (strategy == AUT_STRATEGY_AUTO) strategy = auto_strategy(format, layout, accum);
   const bool dense = layout == AUT_LAYOUT_DENSE;
   const int s = strategy;
@@ -984,16 +1160,17 @@ aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
   // SCALAR runs the LDG kernel with the vector path switched off, so every
   // code goes through the per-value load and decode.
   const bool scalar_only = strategy == AUT_STRATEGY_SCALAR;
-  if (generic_format(format)) {
-    // the generic DOT reads one value per thread: strategy AUTO or SCALAR,
-    // decoder AUTO, DIRECT (bit formats) or FULL_LUT (LNS: host-built table)
+  if (generic_format(format) &&
+      (find_format(format)->family == AUT_FAMILY_LNS || scalar_only)) {
+    // the generic DOT reads one value per thread: LNS formats other than
+    // lns8_r3 / lns16_r11 (decoder AUTO or FULL_LUT: the host-built table),
+    // and the per-value (SCALAR) strategy of the other bit formats
     const format_desc &f = *find_format(format);
     const int direct = f.family == AUT_FAMILY_LNS ? AUT_DECODER_FULL_LUT : AUT_DECODER_DIRECT;
     if ((strategy != AUT_STRATEGY_AUTO && !scalar_only) ||
         (decoder != AUT_DECODER_AUTO && decoder != direct))
       return fail(AUT_ERR_UNSUPPORTED,
-                  "formats without fused kernels take strategy AUTO/SCALAR and their "
-                  "direct (or full-table) decoder");
+                  "this format takes strategy AUTO/SCALAR and its full-table decoder");
     return generic_dot_launch(ws, f, format, layout, accum, x, y, n, batch, bl, results,
                               static_cast<cudaStream_t>(stream), partials, tickets,
                               max_blocks_total);
@@ -1035,6 +1212,7 @@ aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
     if (static_cast<uint64_t>(per_pair) > wanted) per_pair = static_cast<int>(wanted);
     if (per_pair > max_blocks_total) per_pair = max_blocks_total;
     aut::dev::dot_params p = params_for(x, y, n, b0, bl, aligned);
+    if (e.runtime) p.rt = rt_params_for(*find_format(format), accum);
     p.table = table;
     p.partials = partials;
     p.tickets = tickets;

@@ -178,7 +178,7 @@ std::vector<decoder_choice> decoders_for(const std::string &fmt, int32_t accum) 
       return {{AUT_DECODER_AUTO, bytes <= 32 * 1024 ? "full_lut_shared" : "full_lut_global",
                "ordinary", bytes}};
     }
-    return {{AUT_DECODER_AUTO, "generic", "ordinary", 0}};
+    return {{AUT_DECODER_AUTO, "direct_shift", "ordinary", 0}};  // runtime E/M/bias
   }
   if (fmt == "lns8_r3") return {{AUT_DECODER_FULL_LUT, "full_lut_shared", "ordinary", 256 * 32 * t}};
   if (fmt == "lns16_r11") {
