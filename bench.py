@@ -68,7 +68,7 @@ METRIC = "decoded elems/s & HBM GB/s (% of 8 TB/s) at N=2^27/GPU, 1-8 GPUs; norm
 def parse():
     p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=400)
+    p.add_argument("--steps", type=int, default=2000)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="e8-sweep")
@@ -115,6 +115,7 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.lines = []
+        self.first = 0  # samples before this index precede the timed region
 
     def __enter__(self):
         try:
@@ -124,6 +125,10 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            # the timed region starts once nvidia-smi reports (it needs ~0.1 s)
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 5.0 and self.proc.poll() is None:
+                time.sleep(0.01)
         except OSError:
             self.proc = None
         return self
@@ -140,10 +145,15 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
 
+    def mark(self):
+        """Called as the timed region starts."""
+        self.first = len(self.lines)
+
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
+        timed = self.lines[self.first:] or self.lines[-1:]
+        for line in timed:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -356,6 +366,7 @@ def main():
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(physical_gpu(local)) as clocks:
         torch.cuda.synchronize()
+        clocks.mark()
         start.record()
         for _ in range(args.steps):
             step()
