@@ -592,6 +592,15 @@ template <int S, typename T, bool kDense> struct rt_codec {
   }
 };
 
+// Tiles between carries of the FP32 lanes into FP64: at most 32 products per
+// FP32 chain (4 chains; the stated error bound), or, for exact lanes, 16 tiles
+// (far below the 4096 products an exact FP32 lane holds).
+template <class Codec>
+constexpr int flush_every(int values_per_tile) {
+  if (Codec::kExactLanes) return 16;
+  return values_per_tile >= 128 ? 1 : 128 / values_per_tile;
+}
+
 template <class Codec, class Acc>
 __device__ __forceinline__ void flush_tile(Acc &acc, float *lanes) {
   if constexpr (Codec::kExactLanes) {
@@ -642,6 +651,8 @@ __global__ void __launch_bounds__(kThreads)
   const uint64_t tiles = p.vector_ok ? (p.n / P) / tile_packets : 0;
   const uint4 *X = reinterpret_cast<const uint4 *>(xb);
   const uint4 *Y = reinterpret_cast<const uint4 *>(yb);
+  constexpr int kFlush = flush_every<Codec>(P * U);
+  int since_flush = 0;
   for (uint64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
     const uint64_t first = t * tile_packets + threadIdx.x;
     uint4 xv[U][Q], yv[U][Q];
@@ -658,8 +669,12 @@ __global__ void __launch_bounds__(kThreads)
       Codec::template values<P>(reinterpret_cast<const uint32_t *>(xv[u]),
                                 reinterpret_cast<const uint32_t *>(yv[u]), acc,
                                 lanes, smem);
-    flush_tile<Codec>(acc, lanes);
+    if (++since_flush == kFlush) {
+      flush_tile<Codec>(acc, lanes);
+      since_flush = 0;
+    }
   }
+  flush_tile<Codec>(acc, lanes);
 
   ragged_tail<Codec>(xb, xo, yb, yo, tiles * tile_packets * P, p.n, acc, smem);
   const double s = block_sum(acc.value(), scratch);
@@ -781,10 +796,10 @@ __global__ void __launch_bounds__(kThreads)
   const uint64_t mine =
       tiles > blockIdx.x ? (tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
 
-  auto issue = [&](uint64_t k) {
+  auto issue = [&](uint64_t k, uint32_t stage) {  // stage == k % STAGES
     const uint64_t t = blockIdx.x + k * gridDim.x;
-    unsigned char *dst = ring + (k % STAGES) * (2 * TILE_BYTES);
-    uint64_t *bar = &full[k % STAGES];
+    unsigned char *dst = ring + stage * (2 * TILE_BYTES);
+    uint64_t *bar = &full[stage];
     mbar_expect_tx(bar, 2u * TILE_BYTES);
     bulk_load(dst, xb + t * TILE_BYTES, TILE_BYTES, bar);
     bulk_load(dst + TILE_BYTES, yb + t * TILE_BYTES, TILE_BYTES, bar);
@@ -797,16 +812,18 @@ __global__ void __launch_bounds__(kThreads)
   if constexpr (Codec::kTableBytes > 0) Codec::prepare(p, smem);
   __syncthreads();
   if (threadIdx.x == 0)
-    for (uint64_t k = 0; k < mine && k < STAGES; ++k) issue(k);
+    for (uint32_t k = 0; k < mine && k < static_cast<uint32_t>(STAGES); ++k) issue(k, k);
 
   Acc acc;
   float lanes[4] = {0.f, 0.f, 0.f, 0.f};
   bool failed = false;
+  constexpr int kFlush = flush_every<Codec>(shape::VPT);
+  int since_flush = 0;
+  uint32_t stage = 0, phase = 0;  // k % STAGES and (k / STAGES) & 1
   uint64_t k = 0;
   for (; k < mine; ++k) {
-    const bool ok = mbar_wait(&full[k % STAGES], static_cast<uint32_t>((k / STAGES) & 1));
-    const uint32_t *xs =
-        reinterpret_cast<const uint32_t *>(ring + (k % STAGES) * (2 * TILE_BYTES));
+    const bool ok = mbar_wait(&full[stage], phase);
+    const uint32_t *xs = reinterpret_cast<const uint32_t *>(ring + stage * (2 * TILE_BYTES));
     const uint32_t *ys = xs + shape::TILE_WORDS;
 #pragma unroll
     for (int v = 0; v < V / GROUP; ++v) {
@@ -826,7 +843,10 @@ __global__ void __launch_bounds__(kThreads)
       }
       Codec::template values<UV * GROUP>(xw, yw, acc, lanes, smem);
     }
-    flush_tile<Codec>(acc, lanes);
+    if (++since_flush == kFlush) {
+      flush_tile<Codec>(acc, lanes);
+      since_flush = 0;
+    }
     // Every thread is done with this stage (and the exit decision is the
     // same for all threads) before it is refilled.
     if (__syncthreads_or(ok ? 0 : 1)) {
@@ -835,9 +855,14 @@ __global__ void __launch_bounds__(kThreads)
     }
     if (threadIdx.x == 0 && k + STAGES < mine) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(k + STAGES);
+      issue(k + STAGES, stage);
+    }
+    if (++stage == static_cast<uint32_t>(STAGES)) {
+      stage = 0;
+      phase ^= 1u;
     }
   }
+  flush_tile<Codec>(acc, lanes);
   if (failed) {
     // Let the copies this block still has in flight land before it exits.
     if (threadIdx.x == 0) {

@@ -383,9 +383,11 @@ def main():
 
     # per-kernel CUDA-event timing (same stream) for the roofline, for the
     # strategy in use and for each explicit access strategy
-    reps = 20
+    reps = 50
 
     def time_kernel(k, strat, dec=0):
+        launch(k, strat, dec)  # untimed: first-use set-up of this variant
+        torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for _ in range(reps):
