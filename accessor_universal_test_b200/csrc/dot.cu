@@ -139,7 +139,7 @@ struct f64_codec {
 template <int S> struct e2m3_codec {
   static_assert(S == 6 || S == 8, "dense 6-bit or one code per byte");
   static constexpr int kS = S;
-  static constexpr int kU = S == 8 ? 4 : 1;
+  static constexpr int kU = S == 8 ? 4 : 2;
   static constexpr int kTableBytes = 0;
   static constexpr bool kExactLanes = true;
   __device__ static void prepare(const dot_params &, unsigned char *) {}
@@ -685,24 +685,32 @@ __global__ void __launch_bounds__(kThreads)
 // ---------------------------------------------------------------------------
 // TMA strategy: a shared-memory ring fed by cp.async.bulk.
 // ---------------------------------------------------------------------------
-// Geometry of one tile: every thread owns kValuesPerThread consecutive codes
-// in units of UW words (UW = S / gcd(S, 32) is odd, so a warp reading word k
-// of 32 consecutive units hits 32 different banks).
-template <int S, int RING = 64 * 1024, int VPT_ = (S >= 24 ? 16 : (S <= 4 ? 128 : 32))>
+// Geometry of one tile: a unit is UW = S / gcd(S, 32) words holding UV whole
+// codes; every thread owns V units per tile, read GROUP consecutive units
+// (LW words) per shared load.
+// Units read per shared load: 1- and 2-word units four / two at a time (one
+// 16-byte load); odd units of 3 words four at a time (12 words: three 16-byte
+// loads, lanes 48 bytes apart, so a quarter warp covers 32 distinct banks) and
+// of 5, 7 or 9 words two at a time (8-byte loads, lanes 2*UW words apart: a
+// half warp covers 32 distinct banks); longer units one at a time.
+constexpr int tma_group(int uw) {
+  return uw <= 2 ? 4 / uw : (uw == 3 ? 4 : (uw <= 9 ? 2 : 1));
+}
+constexpr int tma_vpt(int s) {
+  const int uw = s / gcd_int(s, 32), uv = s == 64 ? 1 : 32 / gcd_int(s, 32);
+  const int base = s >= 24 ? 16 : (s <= 4 ? 128 : 32);
+  return base >= tma_group(uw) * uv ? base : tma_group(uw) * uv;
+}
+
+template <int S, int RING = 64 * 1024, int VPT_ = tma_vpt(S)>
 struct tma_shape {
   static constexpr int G = gcd_int(S, 32);
   static constexpr int UW = S / G;                 // words per unit
   static constexpr int UV = S == 64 ? 1 : 32 / G;  // codes per unit
   static constexpr int VPT = VPT_;                 // codes per thread per tile
   static constexpr int V = VPT / UV;               // units per thread per tile
-  // Units of one or two words are read four words at a time: one 16-byte
-  // shared load per operand, a quarter warp covering 128 contiguous bytes
-  // (no bank conflicts), and one decode call per four words.  Longer units
-  // have an odd word count and are read word by word, one unit per lane,
-  // which is conflict-free too.
-  static constexpr int GROUP_RAW = UW <= 2 ? 4 / UW : 1;
-  static constexpr int GROUP = GROUP_RAW < V ? GROUP_RAW : V;  // units per load
-  static constexpr int LW = UW * GROUP;              // words per load
+  static constexpr int GROUP = tma_group(UW) < V ? tma_group(UW) : V;  // units per load
+  static constexpr int LW = UW * GROUP;            // words per load
   static constexpr int TILE_WORDS = kThreads * V * UW;
   static constexpr int TILE_BYTES = TILE_WORDS * 4;  // per vector
   static constexpr uint64_t TILE_VALUES = static_cast<uint64_t>(kThreads) * VPT;
@@ -829,11 +837,22 @@ __global__ void __launch_bounds__(kThreads)
     for (int v = 0; v < V / GROUP; ++v) {
       const int u = threadIdx.x + v * kThreads;  // load index
       uint32_t xw[LW], yw[LW];
-      if constexpr (LW == 4) {
-        const uint4 a = reinterpret_cast<const uint4 *>(xs)[u];
-        const uint4 b = reinterpret_cast<const uint4 *>(ys)[u];
-        xw[0] = a.x; xw[1] = a.y; xw[2] = a.z; xw[3] = a.w;
-        yw[0] = b.x; yw[1] = b.y; yw[2] = b.z; yw[3] = b.w;
+      if constexpr (LW % 4 == 0) {
+#pragma unroll
+        for (int q = 0; q < LW / 4; ++q) {
+          const uint4 a = reinterpret_cast<const uint4 *>(xs)[u * (LW / 4) + q];
+          const uint4 b = reinterpret_cast<const uint4 *>(ys)[u * (LW / 4) + q];
+          xw[4 * q] = a.x; xw[4 * q + 1] = a.y; xw[4 * q + 2] = a.z; xw[4 * q + 3] = a.w;
+          yw[4 * q] = b.x; yw[4 * q + 1] = b.y; yw[4 * q + 2] = b.z; yw[4 * q + 3] = b.w;
+        }
+      } else if constexpr (LW % 2 == 0) {
+#pragma unroll
+        for (int q = 0; q < LW / 2; ++q) {
+          const uint2 a = reinterpret_cast<const uint2 *>(xs)[u * (LW / 2) + q];
+          const uint2 b = reinterpret_cast<const uint2 *>(ys)[u * (LW / 2) + q];
+          xw[2 * q] = a.x; xw[2 * q + 1] = a.y;
+          yw[2 * q] = b.x; yw[2 * q + 1] = b.y;
+        }
       } else {
 #pragma unroll
         for (int w = 0; w < LW; ++w) {
@@ -1003,23 +1022,21 @@ kernel_entry pick(int strategy, int accum, int table_kind) {
 // The strategy AUTO resolves to per format and accumulator, chosen from
 // CUDA-event timings of both strategies at N = 2^27 on B200 (packed GB/s,
 // LDG / TMA, FP32 accumulator):
-//   fp32 6916 / 6636     fp64  7106 / 7242     e2m3 5140 / 4642
-//   e8m0 4294 / 5529     e8m1 5517 / 5846     e8m3 5841 / 6090
-//   e8m5 4543 / 6377     bf16 6636 / 6519     e8m15 6417 / 6689
-//   lns8_r3 4835 / 5116 (FP64 accumulator: 3677 / 2444)
-//   lns16_r11 (fused multiply) 4686 / 4589 (FP64: 3710 / 3631)
-// Packets of several 16-byte vectors (S = 9, 10, 12, 14, 24) load strided
-// per thread and stall on the LSU queue; the bulk-copy ring removes that.
-// e2m3 loses more to the staging instructions than it gains; lns8 with FP64
-// has a 64 KiB table, and beside the 64 KiB ring only one block fits an SM.
+//   fp32 7037 / 6776     fp64  7185 / 7312     e2m3 5313 / 5417
+//   e8m0 3988 / 5746     e8m1 5200 / 5931     e8m3 6053 / 6168
+//   e8m5 5344 / 6409     bf16 6682 / 6631     e8m15 6522 / 6810
+//   lns8_r3 4756 / 5567 (FP64 accumulator: 3677 / 2444)
+//   lns16_r11 (fused multiply) 4321 / 4540 (FP64: 3710 / 3631)
+// Packets of several 16-byte vectors (S = 6, 9, 10, 14, 24) load strided per
+// thread and stall on the LSU queue; the bulk-copy ring removes that.  lns8
+// with FP64 has a 64 KiB table, and beside the ring only one block fits an SM.
 int auto_strategy(int32_t format, int32_t layout, int32_t accum) {
   (void)layout;
   switch (format) {
   case AUT_FMT_FP32:
-  case AUT_FMT_E2M3:
-  case AUT_FMT_BF16_E8M7:
-  case AUT_FMT_LNS16_R11: return AUT_STRATEGY_LDG;
+  case AUT_FMT_BF16_E8M7: return AUT_STRATEGY_LDG;
   case AUT_FMT_LNS8_R3:
+  case AUT_FMT_LNS16_R11:
     return accum == AUT_ACCUM_FP32 ? AUT_STRATEGY_TMA : AUT_STRATEGY_LDG;
   default: return AUT_STRATEGY_TMA;
   }
