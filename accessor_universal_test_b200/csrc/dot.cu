@@ -402,9 +402,31 @@ struct lns16_full_codec {
 template <typename T> struct lns16_fused_codec {
   static constexpr int kS = 16;
   static constexpr int kU = 4;
-  static constexpr int kTableBytes = 2048 * static_cast<int>(sizeof(T));
+  static constexpr int kEntry = static_cast<int>(sizeof(T));
+  static constexpr int kTableBytes = 2048 * kEntry + 48;  // table + multipliers
   static constexpr bool kExactLanes = false;
   static constexpr int kMant = sizeof(T) == 4 ? 23 : 20;  // exponent shift in the top word
+
+  // Field moves done as integer multiplies (x * 2^k for left shifts, the
+  // high word of x * 2^k for right shifts, x * 1 + y for adds) run on the
+  // FMA pipe instead of the ALU pipe, which the masks, permutes and logic
+  // of this decode already fill.  The multipliers are read from shared
+  // memory, so the compiler cannot turn them back into shifts.
+  struct multipliers {
+    uint32_t one;      // 1
+    uint32_t k21;      // 2^21: low fraction (bits 0-10) -> bits 21-31, zeros below
+    uint32_t k5;       // 2^5: high exponent (bits 27-31) -> bits 0-4 (high word)
+    uint32_t off;      // 2^(13 + log2 sizeof(T) - 2): bits 21-31 -> byte offset (high word)
+    uint32_t off_hi;   // 2^(16 + log2 sizeof(T)): high fraction -> byte offset (high word)
+    uint32_t exp;      // 2^kMant: exponent -> exponent field
+    uint32_t exp_lo;   // 2^(kMant - 11): low exponent (bits 11-15) -> exponent field
+    uint32_t sign_lo;  // 2^16: bit 15 -> bit 31
+    uint32_t mag;      // 0x7fff7fff: both log fields
+    uint32_t bias;     // 0x40004000: two's complement -> offset binary
+    uint32_t pad[2];
+  };
+  static_assert(sizeof(multipliers) == kTableBytes - 2048 * kEntry, "table layout");
+
   __device__ static void prepare(const dot_params &p, unsigned char *smem) {
     const void *table = p.table;
     const T *g = static_cast<const T *>(table);
@@ -416,6 +438,20 @@ template <typename T> struct lns16_fused_codec {
         const double t = g[e];
         s[e] = __hiloint2double(__double2hiint(t) - (16 << kMant), __double2loint(t));
       }
+    }
+    if (threadIdx.x == 0) {
+      multipliers m{};
+      m.one = 1u;
+      m.k21 = 1u << 21;
+      m.k5 = 1u << 5;
+      m.off = 1u << (kEntry == 4 ? 13 : 14);
+      m.off_hi = 1u << (kEntry == 4 ? 18 : 19);
+      m.exp = 1u << kMant;
+      m.exp_lo = 1u << (kMant - 11);
+      m.sign_lo = 1u << 16;
+      m.mag = 0x7fff7fffu;
+      m.bias = 0x40004000u;
+      *reinterpret_cast<multipliers *>(smem + 2048 * kEntry) = m;
     }
   }
 
@@ -472,27 +508,54 @@ template <typename T> struct lns16_fused_codec {
       acc.mac_d(slot, p, 1.0);
   }
 
+  // product of the pair whose biased log sum sits at h's high/low halfword:
+  // table entry at byte offset `off`, exponent field `ef`, live mask, sign
+  __device__ __forceinline__ static T product_at(const unsigned char *smem, uint32_t off,
+                                                 uint32_t ef, uint32_t mask, uint32_t sign,
+                                                 uint32_t one) {
+    if constexpr (sizeof(T) == 4) {
+      const uint32_t q = __float_as_uint(*reinterpret_cast<const float *>(smem + off)) * one + ef;
+      return __uint_as_float((q & mask) | sign);
+    } else {
+      const double t = *reinterpret_cast<const double *>(smem + off);
+      const uint32_t q = static_cast<uint32_t>(__double2hiint(t)) * one + ef;
+      return __hiloint2double(static_cast<int>((q & mask) | sign),
+                              static_cast<int>(static_cast<uint32_t>(__double2loint(t)) & mask));
+    }
+  }
+
   template <int NV, class Acc>
   __device__ __forceinline__ static void values(const uint32_t *xw,
                                                 const uint32_t *yw, Acc &acc,
                                                 float *,
                                                 const unsigned char *smem) {
     static_assert(NV % 2 == 0, "two codes per word");
-    const T *tab = reinterpret_cast<const T *>(smem);
+    const multipliers m = *reinterpret_cast<const multipliers *>(smem + 2048 * kEntry);
+    constexpr uint32_t kExp = 31u << kMant;   // exponent-field mask
+    constexpr uint32_t kOff = 2047u * kEntry;  // byte-offset mask
     uint32_t nan = 0;
 #pragma unroll
     for (int w = 0; w < NV / 2; ++w) {
       const uint32_t x = xw[w], y = yw[w];
-      const uint32_t bx = (x & 0x7fff7fffu) ^ 0x40004000u;
-      const uint32_t by = (y & 0x7fff7fffu) ^ 0x40004000u;
-      const uint32_t h = bx + by;
+      const uint32_t bx = (x & m.mag) ^ m.bias;  // one three-input logic op each
+      const uint32_t by = (y & m.mag) ^ m.bias;
+      const uint32_t h = bx * m.one + by;
       // bits 15 / 31: that code is not reserved
-      const uint32_t lx = bx + 0x7fff7fffu, ly = by + 0x7fff7fffu;
+      const uint32_t lx = bx * m.one + 0x7fff7fffu, ly = by * m.one + 0x7fff7fffu;
       nan |= (x & ~lx) | (y & ~ly);  // reserved with the sign bit set
       const uint32_t live = lx & ly;
       const uint32_t sg = x ^ y;
-      add(acc, 2 * w, masked(product(h & 0xffffu, (sg << 16) & 0x80000000u, tab), spread<1>(live)));
-      add(acc, 2 * w + 1, masked(product(h >> 16, sg & 0x80000000u, tab), spread<3>(live)));
+      // the high word of (low fraction at bits 21-31, zeros below) * 2^13 is
+      // fraction * 4 (FP64 table: 2^14, fraction * 8), with nothing to mask;
+      // the high fraction has the low exponent below it, so it is masked
+      const uint32_t off_lo = __umulhi(h * m.k21, m.off);
+      const uint32_t off_hi = __umulhi(h, m.off_hi) & kOff;
+      const uint32_t e_lo = (h * m.exp_lo) & kExp;
+      const uint32_t e_hi = __umulhi(h, m.k5) * m.exp;
+      const uint32_t s_lo = (sg * m.sign_lo) & 0x80000000u;
+      const uint32_t s_hi = sg & 0x80000000u;
+      add(acc, 2 * w, product_at(smem, off_lo, e_lo, spread<1>(live), s_lo, m.one));
+      add(acc, 2 * w + 1, product_at(smem, off_hi, e_hi, spread<3>(live), s_hi, m.one));
     }
     if (nan & 0x80008000u) {
       if constexpr (sizeof(T) == 4)
@@ -753,20 +816,27 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
 }
 
 // Returns false when the phase did not complete within kWaitCycles.
+__device__ __forceinline__ bool mbar_try(uint32_t addr, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// The common case (the tile has landed) costs one try_wait; the clock is
+// read only once the first try fails, and then every 32 tries.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
   const uint32_t addr = smem_addr(bar);
+  if (mbar_try(addr, parity)) return true;
   const long long start = clock64();
-  while (true) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(addr), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if (clock64() - start > kWaitCycles) return false;
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try(addr, parity)) return true;
+    if ((i & 31u) == 0u && clock64() - start > kWaitCycles) return false;
   }
 }
 
