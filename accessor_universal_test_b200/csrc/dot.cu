@@ -23,6 +23,7 @@
 
 #include <cstdio>
 #include <cstring>
+#include <type_traits>
 
 namespace aut::dev {
 
@@ -74,15 +75,53 @@ template <int S, int W> struct e8_codec {
   static constexpr bool kExactLanes = false;
   __device__ static void prepare(const dot_params &, unsigned char *) {}
 
+  // With at most 11 mantissa bits the FP32 product of two decoded values is
+  // exact unless it underflows or overflows, so the FP64 accumulator widens
+  // the product (one conversion per pair) instead of both operands (two
+  // conversions, which bound the kernel on the conversion pipe).  A call
+  // whose smallest |product| is below 2^-126 (zeros included) or whose sum is
+  // not finite is redone with both operands widened: the result is the same
+  // FP64 sum of exact products either way.
+  static constexpr bool kProductWidening = W - 9 <= 11;
+
   template <int NV, class Acc>
   __device__ __forceinline__ static void values(const uint32_t *xw,
                                                 const uint32_t *yw, Acc &acc,
                                                 float *, const unsigned char *) {
+    if constexpr (kProductWidening && std::is_same_v<Acc, acc_f64>) {
+      constexpr int C = NV < 16 ? NV : 16;  // values per check
+      static_assert(NV % C == 0, "whole chunks");
 #pragma unroll
-    for (int v = 0; v < NV; ++v) {
-      const float a = __uint_as_float(field_top<S, W>(xw, v));
-      const float b = __uint_as_float(field_top<S, W>(yw, v));
-      acc.mac(v, a, b);
+      for (int c0 = 0; c0 < NV; c0 += C) {
+        double s0 = 0.0, s1 = 0.0;
+        float smallest = __int_as_float(0x7f800000);
+#pragma unroll
+        for (int v = c0; v < c0 + C; ++v) {
+          const float p = __uint_as_float(field_top<S, W>(xw, v)) *
+                          __uint_as_float(field_top<S, W>(yw, v));
+          smallest = fminf(smallest, fabsf(p));
+          if (v & 1)
+            s1 += static_cast<double>(p);
+          else
+            s0 += static_cast<double>(p);
+        }
+        const double s = s0 + s1;
+        if (smallest >= 1.17549435e-38f && fabs(s) <= 1.7976931348623157e308) {
+          acc.add_exact(s);
+        } else {
+#pragma unroll
+          for (int v = c0; v < c0 + C; ++v)
+            acc.mac(v, __uint_as_float(field_top<S, W>(xw, v)),
+                    __uint_as_float(field_top<S, W>(yw, v)));
+        }
+      }
+    } else {
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        const float a = __uint_as_float(field_top<S, W>(xw, v));
+        const float b = __uint_as_float(field_top<S, W>(yw, v));
+        acc.mac(v, a, b);
+      }
     }
   }
 
