@@ -179,16 +179,40 @@ template <int S> struct e2m3_codec {
   static_assert(S == 6 || S == 8, "dense 6-bit or one code per byte");
   static constexpr int kS = S;
   static constexpr int kU = S == 8 ? 4 : 2;
-  static constexpr int kTableBytes = 0;
+  // dense: two multipliers in shared memory (see bytes4)
+  static constexpr int kTableBytes = S == 6 ? 16 : 0;
   static constexpr bool kExactLanes = true;
-  __device__ static void prepare(const dot_params &, unsigned char *) {}
+  __device__ static void prepare(const dot_params &, unsigned char *smem) {
+    if constexpr (S == 6) {
+      if (threadIdx.x == 0) {
+        uint32_t *m = reinterpret_cast<uint32_t *>(smem);
+        m[0] = 1u << 8;
+        m[1] = 1u << 24;
+        m[2] = m[3] = 0u;
+      }
+    }
+  }
 
-  // Codes 4g .. 4g+3 of the word array, one per byte (low 6 bits).
-  __device__ __forceinline__ static uint32_t bytes4(const uint32_t *w, int g) {
+  // Codes 4g .. 4g+3 of the word array, one per byte (low 6 bits).  The
+  // 24-bit groups that start at bit 0 or end at bit 32 of a word are moved by
+  // integer multiplies (the high word of (w * 2^8) * 2^24 is w & 0xffffff; of
+  // w * 2^24, w >> 8), which run on the FMA pipe; the multipliers come from
+  // shared memory, so the compiler keeps them as multiplies instead of
+  // shifts and masks on the busier ALU pipe.
+  __device__ __forceinline__ static uint32_t bytes4(const uint32_t *w, int g,
+                                                    const unsigned char *smem) {
     if constexpr (S == 8) {
       return w[g] & 0x3f3f3f3fu;
     } else {
-      const uint32_t q = field_low<24, 24>(w, g);    // v3 v2 v1 v0, 6 bits each
+      const uint32_t *m = reinterpret_cast<const uint32_t *>(smem);
+      const int b = 24 * g, i = b >> 5, sh = b & 31;
+      uint32_t q;  // v3 v2 v1 v0, 6 bits each
+      if (sh == 0)
+        q = __umulhi(w[i] * m[0], m[1]);
+      else if (sh == 8)
+        q = __umulhi(w[i], m[1]);
+      else
+        q = field_low<24, 24>(w, g);
       const uint32_t p = q + (q & 0x00fff000u) * 15u; // v1v0 -> [0,12), v3v2 -> [16,28)
       return p + (p & 0x0fc00fc0u) * 3u;             // each code at a byte
     }
@@ -200,6 +224,17 @@ template <int S> struct e2m3_codec {
         : "=r"(h2)
         : "h"(static_cast<unsigned short>(two_bytes)));
     return h2;
+  }
+
+  // both byte pairs of a word: the halves are register halves, no shift
+  __device__ __forceinline__ static void to_f16x2x2(uint32_t four, uint32_t &lo,
+                                                    uint32_t &hi) {
+    asm("{\n\t.reg .b16 l, h;\n\t"
+        "mov.b32 {l, h}, %2;\n\t"
+        "cvt.rn.f16x2.e2m3x2 %0, l;\n\t"
+        "cvt.rn.f16x2.e2m3x2 %1, h;\n\t}"
+        : "=r"(lo), "=r"(hi)
+        : "r"(four));
   }
 
   __device__ __forceinline__ static void fma2(float &lo, float &hi, uint32_t x2,
@@ -217,14 +252,15 @@ template <int S> struct e2m3_codec {
   __device__ __forceinline__ static void values(const uint32_t *xw,
                                                 const uint32_t *yw, Acc &,
                                                 float *lanes,
-                                                const unsigned char *) {
+                                                const unsigned char *smem) {
     static_assert(NV % 4 == 0, "e2m3 decodes groups of four codes");
 #pragma unroll
     for (int g = 0; g < NV / 4; ++g) {
-      const uint32_t bx = bytes4(xw, g);
-      const uint32_t by = bytes4(yw, g);
-      fma2(lanes[0], lanes[1], to_f16x2(bx), to_f16x2(by));
-      fma2(lanes[2], lanes[3], to_f16x2(bx >> 16), to_f16x2(by >> 16));
+      uint32_t xl, xh, yl, yh;
+      to_f16x2x2(bytes4(xw, g, smem), xl, xh);
+      to_f16x2x2(bytes4(yw, g, smem), yl, yh);
+      fma2(lanes[0], lanes[1], xl, yl);
+      fma2(lanes[2], lanes[3], xh, yh);
     }
   }
 
