@@ -322,8 +322,8 @@ aut_status make_params(aut_workspace *ws, const format_desc &f, int32_t format,
   p.lns_f32 = nullptr;
   p.lns_f64 = nullptr;
   if (f.family == AUT_FAMILY_LNS) {
-    const lns_tables *t = nullptr;
-    const aut_status st = lns_tables_for(ws, format, &t);
+    const code_tables *t = nullptr;
+    const aut_status st = code_tables_for(ws, format, &t);
     if (st != AUT_OK) return st;
     p.thresholds = t->thresholds;
     p.zero_threshold = t->zero_threshold;

@@ -652,6 +652,61 @@ template <typename T> struct lns16_fused_codec {
   }
 };
 
+// Formats with codes of at most 8 bits and no dedicated codec (bit formats
+// and LNS alike): the full decode table of the format, built on the host
+// from the host decoder, replicated once per lane in shared memory (entry e
+// of lane l at element e*32 + l) so a warp's lookups are conflict-free -- the
+// reference's full_lut_shared decoder (bitwidth_benchmark_kernels.cuh:166-
+// 288).  S is the slot width: the code width when dense, 8 for padded bytes.
+template <int S, typename T> struct lut_codec {
+  static_assert(S >= 2 && S <= 8, "codes of 2 to 8 bits");
+  static constexpr int kS = S;
+  static constexpr int kU = packet_shape<S>::Q == 1 ? 4 : 1;
+  static constexpr int kEntries = 1 << S;
+  static constexpr int kTableBytes = kEntries * 32 * static_cast<int>(sizeof(T));
+  static constexpr bool kExactLanes = false;
+  static constexpr uint32_t kEntryBytes = 32 * sizeof(T);
+
+  __device__ static void prepare(const dot_params &p, unsigned char *smem) {
+    const T *g = static_cast<const T *>(p.table);
+    T *s = reinterpret_cast<T *>(smem);
+    const int entries = 1 << p.rt.bits;  // the format's codes (<= kEntries)
+    for (int e = threadIdx.x; e < entries * 32; e += kThreads) s[e] = g[e >> 5];
+  }
+
+  __device__ __forceinline__ static uint32_t code(const uint32_t *w, int v) {
+    if constexpr (S == 8)
+      return __byte_perm(w[v >> 2], 0u, 0x4440u + (v & 3));
+    else
+      return field_low<S, S>(w, v);
+  }
+
+  template <int NV, class Acc>
+  __device__ __forceinline__ static void values(const uint32_t *xw,
+                                                const uint32_t *yw, Acc &acc,
+                                                float *, const unsigned char *smem) {
+    const uint32_t lane_off = (threadIdx.x & 31) * static_cast<uint32_t>(sizeof(T));
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const T a = *reinterpret_cast<const T *>(smem + (code(xw, v) * kEntryBytes + lane_off));
+      const T b = *reinterpret_cast<const T *>(smem + (code(yw, v) * kEntryBytes + lane_off));
+      if constexpr (sizeof(T) == 4)
+        acc.mac(v, a, b);
+      else
+        acc.mac_d(v, a, b);
+    }
+  }
+
+  template <class Acc>
+  __device__ __forceinline__ static void scalar(const unsigned char *xb, uint64_t i,
+                                                const unsigned char *yb, uint64_t j,
+                                                Acc &acc, const unsigned char *smem) {
+    const T *tab = reinterpret_cast<const T *>(smem) + (threadIdx.x & 31);
+    acc.mac_d(0, static_cast<double>(tab[load_code<S, S>(xb, i) << 5]),
+              static_cast<double>(tab[load_code<S, S>(yb, j) << 5]));
+  }
+};
+
 // The rest of the registry's bit formats (IEEE-like E/M of any width, E0
 // fixed point, FP64 prefixes), decoded by runtime parameters: the code is
 // moved to the top of a word (sign at bit 31), its magnitude shifted right
@@ -1157,6 +1212,31 @@ aut::dev::rt_params rt_params_for(const format_desc &f, int32_t accum) {
   return r;
 }
 
+template <int S>
+kernel_entry lut_entry(int32_t accum, int strategy) {
+  using namespace aut::dev;
+  kernel_entry e = accum == AUT_ACCUM_FP32
+                       ? make_entry<lut_codec<S, float>, acc_f32>(strategy, 1)
+                       : make_entry<lut_codec<S, double>, acc_f64>(strategy, 2);
+  e.runtime = 1;  // prepare() reads the code width from dot_params::rt
+  return e;
+}
+
+// Codes of at most 8 bits: the table-decoded kernels of their slot width.
+kernel_entry lut_lookup(const format_desc &f, int32_t layout, int32_t accum, int strategy) {
+  if (strategy != AUT_STRATEGY_LDG && strategy != AUT_STRATEGY_TMA) return {};
+  switch (layout == AUT_LAYOUT_PADDED ? 8 : f.total_bits) {
+  case 2: return lut_entry<2>(accum, strategy);
+  case 3: return lut_entry<3>(accum, strategy);
+  case 4: return lut_entry<4>(accum, strategy);
+  case 5: return lut_entry<5>(accum, strategy);
+  case 6: return lut_entry<6>(accum, strategy);
+  case 7: return lut_entry<7>(accum, strategy);
+  case 8: return lut_entry<8>(accum, strategy);
+  default: return {};
+  }
+}
+
 template <class Codec>
 kernel_entry pick(int strategy, int accum, int table_kind) {
   return accum == AUT_ACCUM_FP32
@@ -1196,6 +1276,12 @@ kernel_entry lookup(int32_t format, int32_t layout, int32_t accum, int strategy,
                     int decoder = AUT_DECODER_AUTO) {
   using namespace aut::dev;
   if (format > AUT_FMT_LNS16_R11) {
+    const format_desc *f = find_format(format);
+    if (f == nullptr || !generic_dot_ok(*f, accum)) return {};
+    if (f->total_bits <= 8 && (decoder == AUT_DECODER_AUTO || decoder == AUT_DECODER_FULL_LUT))
+      return lut_lookup(*f, layout, accum, strategy == AUT_STRATEGY_AUTO ? AUT_STRATEGY_TMA
+                                                                         : strategy);
+    if (f->family == AUT_FAMILY_LNS) return {};
     if (strategy != AUT_STRATEGY_AUTO && strategy != AUT_STRATEGY_TMA) return {};
     if (decoder != AUT_DECODER_AUTO && decoder != AUT_DECODER_DIRECT) return {};
     return rt_lookup(format, layout, accum);
@@ -1348,7 +1434,8 @@ aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
   // code goes through the per-value load and decode.
   const bool scalar_only = strategy == AUT_STRATEGY_SCALAR;
   if (generic_format(format) &&
-      (find_format(format)->family == AUT_FAMILY_LNS || scalar_only)) {
+      ((find_format(format)->family == AUT_FAMILY_LNS && find_format(format)->total_bits > 8) ||
+       scalar_only)) {
     // the generic DOT reads one value per thread: LNS formats other than
     // lns8_r3 / lns16_r11 (decoder AUTO or FULL_LUT: the host-built table),
     // and the per-value (SCALAR) strategy of the other bit formats
@@ -1372,8 +1459,8 @@ aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
 
   const void *table = nullptr;
   if (e.table_kind != 0) {
-    const lns_tables *t = nullptr;
-    st = lns_tables_for(ws, format, &t);
+    const code_tables *t = nullptr;
+    st = code_tables_for(ws, format, &t);
     if (st != AUT_OK) return st;
     if ((e.table_kind == 3 && !t->split_f32) || (e.table_kind == 4 && !t->split_f64))
       return fail(AUT_ERR_UNSUPPORTED,
@@ -1442,6 +1529,7 @@ aut_status dot_launch_scratch(int sm_count, int32_t format, int32_t layout,
   if (static_cast<uint64_t>(per_pair) > wanted) per_pair = static_cast<int>(wanted);
   if (per_pair < 1) per_pair = 1;
   aut::dev::dot_params p = params_for(x, y, n, 0, bl, aligned);
+  if (e.runtime) p.rt = rt_params_for(*find_format(format), accum);
   p.table = nullptr;
   p.partials = partials;
   p.tickets = tickets;

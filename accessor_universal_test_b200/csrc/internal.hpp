@@ -37,12 +37,14 @@ void clear_error();
   } while (0)
 
 // ---- decode tables kept per workspace ----------------------------------------
-// LNS formats decode through host-built tables (host exp2f / exp2), so that
-// device values are bit-identical to the reference's host decoder.
-struct lns_tables {
+// LNS formats (B <= 16) and bit formats with codes of at most 8 bits decode
+// through tables built on the host from the host decoder (for LNS the
+// reference's exp2f / exp2), so device values are bit-identical to it.
+struct code_tables {
   int ready = 0;
-  float *full_f32 = nullptr;   // 2^B entries (B <= 16)
+  float *full_f32 = nullptr;   // 2^B entries
   double *full_f64 = nullptr;  // 2^B entries
+  // LNS only:
   float *frac_f32 = nullptr;   // 2^R entries: exp2f(f / 2^R)
   double *frac_f64 = nullptr;  // 2^R entries: exp2(f / 2^R)
   double *thresholds = nullptr; // encode thresholds, 2^(B-1) - 2 entries
@@ -68,7 +70,7 @@ struct batch_layout {
   uint64_t x_stride = 0, y_stride = 0;
   uint64_t x_index_stride = 0, y_index_stride = 0;
 };
-constexpr int kLnsFormatsCached = 24;  // every registered LNS format
+constexpr int kTableFormatsCached = 64;  // every table-decoded registered format
 
 } // namespace aut::lib
 
@@ -80,17 +82,18 @@ struct aut_workspace {
   unsigned int *tickets = nullptr; // [kMaxBatchPerLaunch + 1], kept at zero;
                                    // the last word is the sticky status
   std::mutex mutex;
-  int lns_ids[aut::lib::kLnsFormatsCached];
+  int table_ids[aut::lib::kTableFormatsCached];
   aut_workspace() {
-    for (int &id : lns_ids) id = -1;
+    for (int &id : table_ids) id = -1;
   }
-  aut::lib::lns_tables lns[aut::lib::kLnsFormatsCached];
+  aut::lib::code_tables tables[aut::lib::kTableFormatsCached];
 };
 
 namespace aut::lib {
-// Returns the tables of an LNS format, building them on first use.
-aut_status lns_tables_for(aut_workspace *ws, int32_t format_id,
-                          const lns_tables **out);
+// Returns the decode tables of a format (LNS, or a bit format of at most 8
+// bits), building them on first use.
+aut_status code_tables_for(aut_workspace *ws, int32_t format_id,
+                          const code_tables **out);
 } // namespace aut::lib
 
 #endif

@@ -236,8 +236,26 @@ double switch_point(const format_desc &f, int64_t k, double guess) {
   return aut::detail::double_of(lo_bits);
 }
 
-aut_status build_lns_tables(const format_desc &f, lns_tables &t) {
+aut_status build_code_tables(const format_desc &f, code_tables &t) {
   const int Bb = f.total_bits, R = f.exponent_bits;
+  if (f.family != AUT_FAMILY_LNS) {
+    // bit formats: the full table of every code (FP32: the value narrowed,
+    // exact where the format's values are FP32 values)
+    if (Bb > 8) return fail(AUT_ERR_UNSUPPORTED, "decode tables cover bit formats of <= 8 bits");
+    const size_t full = size_t{1} << Bb;
+    std::vector<float> full32(full);
+    std::vector<double> full64(full);
+    for (size_t r = 0; r < full; ++r) {
+      full64[r] = decode_host(f, static_cast<uint32_t>(r));
+      full32[r] = static_cast<float>(full64[r]);
+    }
+    AUT_CUDA_TRY(cudaMalloc(&t.full_f32, full * sizeof(float)));
+    AUT_CUDA_TRY(cudaMalloc(&t.full_f64, full * sizeof(double)));
+    AUT_CUDA_TRY(cudaMemcpy(t.full_f32, full32.data(), full * sizeof(float), cudaMemcpyHostToDevice));
+    AUT_CUDA_TRY(cudaMemcpy(t.full_f64, full64.data(), full * sizeof(double), cudaMemcpyHostToDevice));
+    t.ready = 1;
+    return AUT_OK;
+  }
   if (Bb > 16)
     return fail(AUT_ERR_UNSUPPORTED, "device LNS tables cover B <= 16 bits");
   const size_t full = size_t{1} << Bb;
@@ -294,13 +312,13 @@ aut_status build_lns_tables(const format_desc &f, lns_tables &t) {
   return AUT_OK;
 }
 
-void free_lns_tables(lns_tables &t) {
+void free_code_tables(code_tables &t) {
   cudaFree(t.full_f32);
   cudaFree(t.full_f64);
   cudaFree(t.frac_f32);
   cudaFree(t.frac_f64);
   cudaFree(t.thresholds);
-  t = lns_tables{};
+  t = code_tables{};
 }
 
 // Makes ws->device current for the scope of a call and restores the caller's.
@@ -319,28 +337,31 @@ struct device_scope {
 
 } // namespace
 
-aut_status lns_tables_for(aut_workspace *ws, int32_t format_id,
-                          const lns_tables **out) {
+aut_status code_tables_for(aut_workspace *ws, int32_t format_id,
+                          const code_tables **out) {
   const format_desc *f = find_format(format_id);
-  if (f == nullptr || f->family != AUT_FAMILY_LNS)
-    return fail(AUT_ERR_INVALID_ARGUMENT, "not an LNS format");
+  if (f == nullptr ||
+      !(f->family == AUT_FAMILY_LNS ||
+        ((f->family == AUT_FAMILY_BINARY || f->family == AUT_FAMILY_FP64_PREFIX) &&
+         f->total_bits <= 8)))
+    return fail(AUT_ERR_INVALID_ARGUMENT, "no decode tables for this format");
   std::lock_guard<std::mutex> lock(ws->mutex);
   int slot = -1;
-  for (int k = 0; k < kLnsFormatsCached; ++k) {
-    if (ws->lns_ids[k] == format_id) {
-      *out = &ws->lns[k];
+  for (int k = 0; k < kTableFormatsCached; ++k) {
+    if (ws->table_ids[k] == format_id) {
+      *out = &ws->tables[k];
       return AUT_OK;
     }
-    if (slot < 0 && ws->lns_ids[k] < 0) slot = k;
+    if (slot < 0 && ws->table_ids[k] < 0) slot = k;
   }
-  if (slot < 0) return fail(AUT_ERR_TOO_LARGE, "too many LNS formats in one workspace");
-  const aut_status st = build_lns_tables(*f, ws->lns[slot]);
+  if (slot < 0) return fail(AUT_ERR_TOO_LARGE, "too many table-decoded formats in one workspace");
+  const aut_status st = build_code_tables(*f, ws->tables[slot]);
   if (st != AUT_OK) {
-    free_lns_tables(ws->lns[slot]);
+    free_code_tables(ws->tables[slot]);
     return st;
   }
-  ws->lns_ids[slot] = format_id;
-  *out = &ws->lns[slot];
+  ws->table_ids[slot] = format_id;
+  *out = &ws->tables[slot];
   return AUT_OK;
 }
 
@@ -457,8 +478,8 @@ aut_status aut_workspace_destroy(aut_workspace *ws) {
   if (ws == nullptr) return AUT_OK;
   {
     device_scope scope(ws->device);
-    for (int k = 0; k < kLnsFormatsCached; ++k)
-      if (ws->lns_ids[k] >= 0) free_lns_tables(ws->lns[k]);
+    for (int k = 0; k < kTableFormatsCached; ++k)
+      if (ws->table_ids[k] >= 0) free_code_tables(ws->tables[k]);
     cudaFree(ws->partials);
     cudaFree(ws->tickets);
   }
@@ -471,11 +492,14 @@ aut_status aut_workspace_prepare(aut_workspace *ws, int32_t format) {
   if (ws == nullptr) return fail(AUT_ERR_INVALID_ARGUMENT, "workspace is NULL");
   const format_desc *f = find_format(format);
   if (f == nullptr) return fail(AUT_ERR_INVALID_ARGUMENT, "unknown format id");
-  if (f->family != AUT_FAMILY_LNS) return AUT_OK;
+  const bool narrow_bits = format > AUT_FMT_LNS16_R11 && f->total_bits <= 8 &&
+                           (f->family == AUT_FAMILY_BINARY ||
+                            f->family == AUT_FAMILY_FP64_PREFIX);
+  if (f->family != AUT_FAMILY_LNS && !narrow_bits) return AUT_OK;
   device_scope scope(ws->device);
   AUT_CUDA_TRY(scope.err);
-  const lns_tables *t = nullptr;
-  return lns_tables_for(ws, format, &t);
+  const code_tables *t = nullptr;
+  return code_tables_for(ws, format, &t);
 }
 
 aut_status aut_workspace_info(const aut_workspace *ws, int32_t *sm_count,

@@ -173,6 +173,13 @@ std::vector<decoder_choice> decoders_for(const std::string &fmt, int32_t accum) 
     const int32_t fid = aut_format_id(fmt.c_str());
     int32_t family = 0, bits = 0, e = 0, fin = 0;
     aut_format_info(fid, &family, &bits, &e, &fin);
+    if (bits <= 8)  // table decode (every family), and the runtime shift for bit formats
+      return family == AUT_FAMILY_LNS
+                 ? std::vector<decoder_choice>{{AUT_DECODER_FULL_LUT, "full_lut_shared",
+                                                "ordinary", (1 << bits) * 32 * t}}
+                 : std::vector<decoder_choice>{{AUT_DECODER_FULL_LUT, "full_lut_shared",
+                                                "ordinary", (1 << bits) * 32 * t},
+                                               {AUT_DECODER_DIRECT, "direct_shift", "ordinary", 0}};
     if (family == AUT_FAMILY_LNS) {
       const int bytes = (1 << bits) * t;
       return {{AUT_DECODER_AUTO, bytes <= 32 * 1024 ? "full_lut_shared" : "full_lut_global",

@@ -50,8 +50,11 @@ def test_every_registered_format_has_a_dot(autlib):
 
 
 @pytest.mark.parametrize("layout", [0, 1])
-@pytest.mark.parametrize("strategy", [0, 3])  # AUTO (runtime-decoder TMA kernels), SCALAR
-def test_generic_dot_matches_oracle_on_every_format(ws, orc, autlib, layout, strategy):
+# AUTO (table decode up to 8 bits, runtime-decoder TMA kernels above), SCALAR,
+# and the runtime decoder forced on every bit format (DIRECT)
+@pytest.mark.parametrize("strategy,decoder", [(0, 0), (3, 0), (0, 1)])
+def test_generic_dot_matches_oracle_on_every_format(ws, orc, autlib, layout, strategy,
+                                                    decoder):
     import torch
     from accessor_universal_test_b200 import _lib
     checked = 0
@@ -59,7 +62,7 @@ def test_generic_dot_matches_oracle_on_every_format(ws, orc, autlib, layout, str
         fid = _lib.format_id(name)
         for n in (1, 4099, 65536 + 13):
             accs = [a for a in (0, 1) if autlib.aut_dot_supported(fid, layout, a)]
-            if not accs:
+            if not accs or (decoder == 1 and _lib.format_info(fid)[0] == _lib.FAMILY_LNS):
                 continue
             _, desc, codes, (x, y) = _pair(ws, orc, name, layout, n)
             (d, s) = orc.dot_codes(desc, codes[0], codes[1], threads=4)
@@ -68,7 +71,7 @@ def test_generic_dot_matches_oracle_on_every_format(ws, orc, autlib, layout, str
             for acc in accs:
                 res = torch.full((1,), float("nan"), dtype=torch.float64, device="cuda")
                 ws.dot(fid, layout, acc, x.data_ptr(), y.data_ptr(), n, res.data_ptr(),
-                       strategy=strategy)
+                       strategy=strategy, decoder=decoder)
                 torch.cuda.synchronize()
                 got = res.item()
                 if not np.isfinite(float(ref)):
@@ -109,9 +112,10 @@ EXHAUSTIVE = ["e1m0", "e2m0", "e3m0", "e7m0", "fp4_e2m1", "e0m7", "e2m5", "e3m4"
 @pytest.mark.parametrize("layout", [0, 1])
 def test_runtime_decoder_on_every_code(ws, orc, autlib, name, layout):
     """Every code (2^16 random codes above 16 bits) times the code nearest
-    1.0, as one-value DOTs of a batch: zeros, subnormals, the largest values,
-    inf and NaN of every exponent width against the oracle's decode, bit for
-    bit."""
+    1.0, as a one-column GEMV (row r = code r times the vector's one code):
+    zeros, subnormals, the largest values, inf and NaN of every exponent
+    width against the oracle's decode, bit for bit, through the table decoder
+    (codes of up to 8 bits) and the runtime-shift decoder."""
     import torch
     from accessor_universal_test_b200 import _lib
     fid = _lib.format_id(name)
@@ -122,41 +126,31 @@ def test_runtime_decoder_on_every_code(ws, orc, autlib, name, layout):
     else:
         codes = np.random.default_rng(9).integers(0, 1 << bits, 1 << 16,
                                                   dtype=np.uint64).astype(np.uint32)
-    one = orc.encode(desc, [1.0])[0]
-    stride = 16
-    per = _lib.storage_bytes(fid, layout, 1)
-    assert per <= stride
-    # one one-value stream per 16-byte slot: the code in the low bits of the
-    # slot's first word (dense: the guard word after it stays zero; padded:
-    # the container), as aut_pack_host lays out a single value
-    single = np.zeros(per, np.uint8)
-    one_code = np.array([one], np.uint32)
-    _lib.check(_lib.load().aut_pack_host(fid, layout, one_code.ctypes.data, 1,
-                                         single.ctypes.data))
-    assert int.from_bytes(single.tobytes(), "little") == int(one)
-    xb = np.zeros((codes.size, stride // 4), np.uint32)
-    yb = np.zeros((codes.size, stride // 4), np.uint32)
-    xb[:, 0] = codes
-    yb[:, 0] = one
-    xt, yt = torch.from_numpy(xb).cuda(), torch.from_numpy(yb).cuda()
+    one = np.array(orc.encode(desc, [1.0]), np.uint32)
+    mat = np.zeros(_lib.storage_bytes(fid, layout, codes.size), np.uint8)
+    vec = np.zeros(_lib.storage_bytes(fid, layout, 1), np.uint8)
+    _lib.check(_lib.load().aut_pack_host(fid, layout, codes.ctypes.data, codes.size,
+                                         mat.ctypes.data))
+    _lib.check(_lib.load().aut_pack_host(fid, layout, one.ctypes.data, 1, vec.ctypes.data))
+    mt, vt = torch.from_numpy(mat).cuda(), torch.from_numpy(vec).cuda()
+    decoders = [0, 1] if bits <= 8 else [0]
     for acc in (0, 1):
         if not autlib.aut_dot_supported(fid, layout, acc):
             continue
-        out = torch.full((codes.size,), 7.0, dtype=torch.float64, device="cuda")
-        ws.dot_batched(fid, layout, acc, xt.data_ptr(), yt.data_ptr(), 1, codes.size, stride,
-                       out.data_ptr())
-        torch.cuda.synchronize()
-        got = out.cpu().numpy()
         dec = orc.decode_f32 if acc == 0 else orc.decode_f64
         # the one-value DOT is the product of the two decoded values, formed
-        # in FP64 (exact for FP32 values; one rounding for the widest codes),
-        # as the ragged-tail path forms it; formats without 1.0 (e1m0 rounds
-        # it to inf) still check every code
+        # in FP64 (exact for FP32 values; one rounding for the widest codes);
+        # formats without 1.0 (e1m0 rounds it to inf) still check every code
         with np.errstate(invalid="ignore", over="ignore"):
-            want = (dec(desc, codes).astype(np.float64) *
-                    np.float64(dec(desc, np.array([one], np.uint32))[0]))
+            want = dec(desc, codes).astype(np.float64) * np.float64(dec(desc, one)[0])
         nan = np.isnan(want)
-        assert np.array_equal(np.isnan(got), nan), (name, acc)
-        ok = got[~nan] == want[~nan]  # +-0 compare equal: the sum starts at +0
-        assert ok.all(), (name, acc, codes[~nan][~ok][:5], got[~nan][~ok][:5],
-                          want[~nan][~ok][:5])
+        for decoder in decoders:
+            out = torch.full((codes.size,), 7.0, dtype=torch.float64, device="cuda")
+            ws.gemv(fid, layout, acc, mt.data_ptr(), vt.data_ptr(), codes.size, 1,
+                    out.data_ptr(), decoder=decoder)
+            torch.cuda.synchronize()
+            got = out.cpu().numpy()
+            assert np.array_equal(np.isnan(got), nan), (name, acc, decoder)
+            ok = got[~nan] == want[~nan]  # +-0 compare equal: the sum starts at +0
+            assert ok.all(), (name, acc, decoder, codes[~nan][~ok][:5], got[~nan][~ok][:5],
+                              want[~nan][~ok][:5])

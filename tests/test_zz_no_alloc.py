@@ -24,7 +24,8 @@ def _noalloc(fid, layout, accum, x_ptr, y_ptr, n, batch, stride, res_ptr):
                                        stride, res_ptr, None)
 
 
-@pytest.mark.parametrize("name", ["e8m0", "e8m15", "e2m3", "bf16_e8m7", "fp32", "fp64"])
+@pytest.mark.parametrize("name", ["e8m0", "e8m15", "e2m3", "bf16_e8m7", "fp32", "fp64",
+                                  "e5m11", "e9m22"])
 def test_noalloc_dot_matches_workspace_dot_twice_in_a_row(ws, orc, name):
     import torch
     from accessor_universal_test_b200 import _lib
@@ -32,7 +33,8 @@ def test_noalloc_dot_matches_workspace_dot_twice_in_a_row(ws, orc, name):
     n = (1 << 21) + 77
     x, y = device_pair(ws, name, _lib.DENSE, n)
     _, ref_abs = oracle_dot(orc, name, n)
-    for accum in ([1] if name == "fp64" else [0, 1]):
+    accums = [a for a in (0, 1) if _lib.load().aut_dot_supported(fid, _lib.DENSE, a)]
+    for accum in accums:
         want = gpu_dot(ws, name, _lib.DENSE, accum, x, y, n)
         for call in range(2):
             res = torch.full((1,), float("nan"), dtype=torch.float64, device="cuda")
