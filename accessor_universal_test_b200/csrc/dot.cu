@@ -919,8 +919,23 @@ struct tma_shape {
 // -- more warps to hide the table lookups' latency -- fit an SM beside the
 // table (lns8_r3, FP32: 5116 -> 5432 GB/s; 16-bit codes keep two 32 KiB
 // stages, since halving their tiles cost 5 %).
-template <class Codec>
-using tma_shape_of = tma_shape<Codec::kS, ((Codec::kTableBytes > 1024) ? 32 * 1024 : 64 * 1024)>;
+// Ring per slot width, from a sweep of 48-200 KiB on B200 (N = 2^27, FP32
+// accumulator, GB/s at 64 KiB -> chosen): 9 bits 5773 -> 6118 (160 KiB),
+// 10 bits 5882 -> 6328 (128), 12 bits 6182 -> 6418 (128), 14 bits 6414 ->
+// 6514 (160), 24 bits 6829 -> 6895 (128); 6 bits keeps 64 KiB (5429; 4266 at
+// 128).  The winners hold one block per SM with four to six stages in flight.
+// The FP64 accumulator keeps 64 KiB: its longer per-pair work wants more
+// warps instead (e8m0 5751 at 64 KiB, 4748 at 160).
+constexpr int tma_ring(int s, bool fp64) {
+  if (fp64) return 64 * 1024;
+  return s == 9 || s == 14 ? 160 * 1024 : (s == 10 || s == 12 || s == 24 ? 128 * 1024 : 64 * 1024);
+}
+
+template <class Codec, class Acc>
+using tma_shape_of =
+    tma_shape<Codec::kS, ((Codec::kTableBytes > 1024)
+                              ? 32 * 1024
+                              : tma_ring(Codec::kS, std::is_same_v<Acc, acc_f64>))>;
 
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 2 GHz
 
@@ -984,7 +999,7 @@ __global__ void __launch_bounds__(kThreads)
     dot_tma_kernel(const dot_params p) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ double scratch[kThreads / 32];
-  using shape = tma_shape_of<Codec>;
+  using shape = tma_shape_of<Codec, Acc>;
   constexpr int UV = shape::UV;
   constexpr int V = shape::V;
   constexpr int GROUP = shape::GROUP;
@@ -1125,7 +1140,7 @@ kernel_entry make_entry(int strategy, int table_kind) {
   e.stride = Codec::kS;
   e.table_kind = table_kind;
   if (strategy == AUT_STRATEGY_TMA) {
-    using shape = aut::dev::tma_shape_of<Codec>;
+    using shape = aut::dev::tma_shape_of<Codec, Acc>;
     e.fn = aut::dev::dot_tma_kernel<Codec, Acc>;
     e.smem = Codec::kTableBytes + shape::STAGES * 2 * shape::TILE_BYTES;
     e.tile_values = shape::TILE_VALUES;
@@ -1142,7 +1157,7 @@ kernel_entry make_entry(int strategy, int table_kind) {
 // LDG thread's registers).
 template <class Codec, class Acc>
 kernel_entry make_tma_entry() {
-  using shape = aut::dev::tma_shape_of<Codec>;
+  using shape = aut::dev::tma_shape_of<Codec, Acc>;
   kernel_entry e;
   e.stride = Codec::kS;
   e.fn = aut::dev::dot_tma_kernel<Codec, Acc>;
@@ -1247,9 +1262,9 @@ kernel_entry pick(int strategy, int accum, int table_kind) {
 // The strategy AUTO resolves to per format and accumulator, chosen from
 // CUDA-event timings of both strategies at N = 2^27 on B200 (packed GB/s,
 // LDG / TMA, FP32 accumulator):
-//   fp32 7037 / 6776     fp64  7185 / 7312     e2m3 5313 / 5417
-//   e8m0 3988 / 5746     e8m1 5200 / 5931     e8m3 6053 / 6168
-//   e8m5 5344 / 6409     bf16 6682 / 6631     e8m15 6522 / 6810
+//   fp32 7037 / 6776     fp64  7185 / 7312     e2m3 5414 / 5422
+//   e8m0 3886 / 6122     e8m1 5272 / 6333     e8m3 5995 / 6474
+//   e8m5 5366 / 6525     bf16 6651 / 6545     e8m15 6532 / 6874
 //   lns8_r3 4756 / 5567 (FP64 accumulator: 3677 / 2444)
 //   lns16_r11 (fused multiply) 4321 / 4540 (FP64: 3710 / 3631)
 // Packets of several 16-byte vectors (S = 6, 9, 10, 14, 24) load strided per
