@@ -931,11 +931,23 @@ constexpr int tma_ring(int s, bool fp64) {
   return s == 9 || s == 14 ? 160 * 1024 : (s == 10 || s == 12 || s == 24 ? 128 * 1024 : 64 * 1024);
 }
 
-template <class Codec, class Acc>
+// A batch of pairs -- rows of a GEMV among them -- gives every pair a short
+// stream that a deep ring with one block per SM starts slowly (E8 GEMV rows,
+// 1024 x 2^17: 2377 GB/s at 160 KiB, 3876 at 64 KiB), so batched launches
+// run a second instantiation with the 64 KiB ring (`Short`). The ring depth
+// stays a compile-time constant: read from the launch parameters instead,
+// it cost the 10-bit codes 14 % (6337 -> 5475 GB/s).
+template <class Codec, class Acc, bool Short = false>
 using tma_shape_of =
     tma_shape<Codec::kS, ((Codec::kTableBytes > 1024)
                               ? 32 * 1024
-                              : tma_ring(Codec::kS, std::is_same_v<Acc, acc_f64>))>;
+                              : (Short ? 64 * 1024
+                                       : tma_ring(Codec::kS, std::is_same_v<Acc, acc_f64>)))>;
+
+// Whether the codec's single-DOT ring is deeper than the batched one.
+template <class Codec, class Acc>
+constexpr bool has_short_ring =
+    tma_shape_of<Codec, Acc, false>::STAGES != tma_shape_of<Codec, Acc, true>::STAGES;
 
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 2 GHz
 
@@ -994,12 +1006,12 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src,
       : "memory");
 }
 
-template <class Codec, class Acc>
+template <class Codec, class Acc, bool Short = false>
 __global__ void __launch_bounds__(kThreads)
     dot_tma_kernel(const dot_params p) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ double scratch[kThreads / 32];
-  using shape = tma_shape_of<Codec, Acc>;
+  using shape = tma_shape_of<Codec, Acc, Short>;
   constexpr int UV = shape::UV;
   constexpr int V = shape::V;
   constexpr int GROUP = shape::GROUP;
@@ -1132,7 +1144,23 @@ struct kernel_entry {
   uint64_t tile_values = 0;  // codes per block-tile of the vector path
   int blocks_per_sm = 0;
   int runtime = 0;      // rt_codec: dot_params::rt carries the format
+  kernel_fn batch_fn = nullptr;  // TMA: the short-ring kernel for batches
+  int batch_smem = 0;
 };
+
+template <class Codec, class Acc>
+void set_tma_kernels(kernel_entry &e) {
+  using shape = aut::dev::tma_shape_of<Codec, Acc>;
+  e.fn = aut::dev::dot_tma_kernel<Codec, Acc>;
+  e.smem = Codec::kTableBytes + shape::STAGES * 2 * shape::TILE_BYTES;
+  e.tile_values = shape::TILE_VALUES;
+  if constexpr (aut::dev::has_short_ring<Codec, Acc>) {
+    using batch_shape = aut::dev::tma_shape_of<Codec, Acc, true>;
+    static_assert(batch_shape::TILE_VALUES == shape::TILE_VALUES, "same tiles");
+    e.batch_fn = aut::dev::dot_tma_kernel<Codec, Acc, true>;
+    e.batch_smem = Codec::kTableBytes + batch_shape::STAGES * 2 * batch_shape::TILE_BYTES;
+  }
+}
 
 template <class Codec, class Acc>
 kernel_entry make_entry(int strategy, int table_kind) {
@@ -1140,10 +1168,7 @@ kernel_entry make_entry(int strategy, int table_kind) {
   e.stride = Codec::kS;
   e.table_kind = table_kind;
   if (strategy == AUT_STRATEGY_TMA) {
-    using shape = aut::dev::tma_shape_of<Codec, Acc>;
-    e.fn = aut::dev::dot_tma_kernel<Codec, Acc>;
-    e.smem = Codec::kTableBytes + shape::STAGES * 2 * shape::TILE_BYTES;
-    e.tile_values = shape::TILE_VALUES;
+    set_tma_kernels<Codec, Acc>(e);
   } else {
     e.fn = aut::dev::dot_ldg_kernel<Codec, Acc>;
     e.smem = Codec::kTableBytes;
@@ -1157,12 +1182,9 @@ kernel_entry make_entry(int strategy, int table_kind) {
 // LDG thread's registers).
 template <class Codec, class Acc>
 kernel_entry make_tma_entry() {
-  using shape = aut::dev::tma_shape_of<Codec, Acc>;
   kernel_entry e;
   e.stride = Codec::kS;
-  e.fn = aut::dev::dot_tma_kernel<Codec, Acc>;
-  e.smem = Codec::kTableBytes + shape::STAGES * 2 * shape::TILE_BYTES;
-  e.tile_values = shape::TILE_VALUES;
+  set_tma_kernels<Codec, Acc>(e);
   e.runtime = 1;
   return e;
 }
@@ -1469,6 +1491,10 @@ aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
   if (e.fn == nullptr)
     return fail(AUT_ERR_UNSUPPORTED,
                 "no fused DOT kernel for this format/layout/accumulator/decoder");
+  if (batch > 1 && e.batch_fn != nullptr) {
+    e.fn = e.batch_fn;
+    e.smem = e.batch_smem;
+  }
   aut_status st = blocks_per_sm(e);
   if (st != AUT_OK) return st;
 
@@ -1531,6 +1557,10 @@ aut_status dot_launch_scratch(int sm_count, int32_t format, int32_t layout,
   if (e.table_kind != 0)
     return fail(AUT_ERR_UNSUPPORTED,
                 "this format decodes through tables kept in a workspace; use aut_dot");
+  if (batch > 1 && e.batch_fn != nullptr) {
+    e.fn = e.batch_fn;
+    e.smem = e.batch_smem;
+  }
   aut_status st = blocks_per_sm(e);
   if (st != AUT_OK) return st;
   const bool aligned = vector_path_ok(x, y, batch, bl);
