@@ -25,7 +25,7 @@ ACC_FP32, ACC_FP64 = 0, 1
 TARGET_FP32, TARGET_FP64 = 0, 1
 STRATEGY_AUTO, STRATEGY_LDG, STRATEGY_TMA, STRATEGY_SCALAR = 0, 1, 2, 3
 (DECODER_AUTO, DECODER_DIRECT, DECODER_FULL_LUT, DECODER_FRACTION_LUT,
- DECODER_FRACTION_LUT_FUSED) = range(5)
+ DECODER_FRACTION_LUT_FUSED, DECODER_FUSED_SUM_LUT) = range(6)
 STATUS_WAIT_TIMEOUT = 1
 GEN_SIGNED_UNIT_F64, GEN_SIGNED_UNIT_F32, GEN_NORMAL, GEN_LNS_CANCEL, GEN_POSITIVE_UNIT_F64 = range(5)
 

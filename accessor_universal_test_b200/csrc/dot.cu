@@ -332,6 +332,115 @@ template <typename T> struct lns8_codec {
   }
 };
 
+// lns8_r3 with the fused-sum decoder (fused_sum_lut_shared,
+// lns_decoder_strategies.cuh:327-347): the two log codes are added and one
+// lookup in a table of every product magnitude serves the pair.  Each 7-bit
+// log code is biased by 2^6 (reserved code -> 0, finite codes -> [1, 127]),
+// so one 32-bit add sums the four byte lanes of a word pair without a carry
+// crossing them, and byte k of the sum indexes the table directly (entry i
+// = T(exp2((i - 128) / 8)), the reference's product table shifted by two
+// slots).  The table is replicated per lane (entry i of lane l at i * 32 +
+// l), so the lookups of a warp never share a bank.  Reserved codes follow
+// lns::multiply_codes (lns_benchmark_core.hpp:241-254) without branches:
+// adding 0x7f to a biased byte sets its top bit exactly when the code is not
+// reserved, a sign-replicating byte permute spreads that bit into a mask that
+// zeroes products with a zero operand, and a reserved code with its sign bit
+// set (NaN) raises a flag that makes the DOT NaN.
+template <typename T> struct lns8_fused_codec {
+  static constexpr int kS = 8;
+  static constexpr int kU = 4;
+  static constexpr int kEntry = static_cast<int>(sizeof(T));
+  static constexpr int kTableBytes = 256 * 32 * kEntry;
+  static constexpr bool kExactLanes = false;
+
+  __device__ static void prepare(const dot_params &p, unsigned char *smem) {
+    const T *g = static_cast<const T *>(p.table);
+    T *s = reinterpret_cast<T *>(smem);
+    for (int e = threadIdx.x; e < 256 * 32; e += kThreads) s[e] = g[e >> 5];
+  }
+
+  template <int K> __device__ __forceinline__ static uint32_t spread(uint32_t v) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(v), "r"(0u), "n"(0x8888 + 0x1111 * K));
+    return r;
+  }
+
+  // entry `index` of this lane's copy, zeroed unless `mask`, sign bit `sign`
+  __device__ __forceinline__ static T product(const unsigned char *smem, uint32_t index,
+                                              uint32_t lane_off, uint32_t mask, uint32_t sign) {
+    const unsigned char *at = smem + (index * (32 * kEntry) + lane_off);
+    if constexpr (sizeof(T) == 4) {
+      const uint32_t t = *reinterpret_cast<const uint32_t *>(at);
+      return __uint_as_float((t & mask) | sign);
+    } else {
+      const uint2 t = *reinterpret_cast<const uint2 *>(at);
+      return __hiloint2double(static_cast<int>((t.y & mask) | sign), static_cast<int>(t.x & mask));
+    }
+  }
+
+  template <class Acc>
+  __device__ __forceinline__ static void add(Acc &acc, int slot, T p) {
+    if constexpr (sizeof(T) == 4)
+      acc.mac(slot, p, 1.0f);
+    else
+      acc.mac_d(slot, p, 1.0);
+  }
+
+  template <int NV, class Acc>
+  __device__ __forceinline__ static void values(const uint32_t *xw,
+                                                const uint32_t *yw, Acc &acc,
+                                                float *,
+                                                const unsigned char *smem) {
+    static_assert(NV % 4 == 0, "four codes per word");
+    const uint32_t lane_off = (threadIdx.x & 31) * static_cast<uint32_t>(kEntry);
+    uint32_t nan = 0;
+#pragma unroll
+    for (int w = 0; w < NV / 4; ++w) {
+      const uint32_t x = xw[w], y = yw[w];
+      const uint32_t bx = (x & 0x7f7f7f7fu) ^ 0x40404040u;
+      const uint32_t by = (y & 0x7f7f7f7fu) ^ 0x40404040u;
+      const uint32_t h = bx + by;  // byte k: biased product log of pair k
+      // bit 7 of each byte: that code is not reserved
+      const uint32_t lx = bx + 0x7f7f7f7fu, ly = by + 0x7f7f7f7fu;
+      nan |= (x & ~lx) | (y & ~ly);  // reserved with the sign bit set
+      const uint32_t live = lx & ly;
+      const uint32_t sg = x ^ y;  // product signs at bits 7, 15, 23, 31
+      add(acc, 4 * w + 0, product(smem, __byte_perm(h, 0u, 0x4440u), lane_off,
+                                  spread<0>(live), (sg << 24) & 0x80000000u));
+      add(acc, 4 * w + 1, product(smem, __byte_perm(h, 0u, 0x4441u), lane_off,
+                                  spread<1>(live), (sg << 16) & 0x80000000u));
+      add(acc, 4 * w + 2, product(smem, __byte_perm(h, 0u, 0x4442u), lane_off,
+                                  spread<2>(live), (sg << 8) & 0x80000000u));
+      add(acc, 4 * w + 3, product(smem, h >> 24, lane_off, spread<3>(live),
+                                  sg & 0x80000000u));
+    }
+    if (nan & 0x80808080u) {
+      if constexpr (sizeof(T) == 4)
+        add(acc, 0, __uint_as_float(0x7fc00000u));
+      else
+        add(acc, 0, __hiloint2double(0x7ff80000, 0));
+    }
+  }
+
+  template <class Acc>
+  __device__ __forceinline__ static void scalar(const unsigned char *xb, uint64_t i,
+                                                const unsigned char *yb, uint64_t j,
+                                                Acc &acc,
+                                                const unsigned char *smem) {
+    const uint32_t cx = load_code<8, 8>(xb, i), cy = load_code<8, 8>(yb, j);
+    const uint32_t bx = (cx & 0x7fu) ^ 0x40u, by = (cy & 0x7fu) ^ 0x40u;
+    double v;
+    if ((bx == 0 && (cx & 0x80u)) || (by == 0 && (cy & 0x80u))) {
+      v = __hiloint2double(0x7ff80000, 0);
+    } else {
+      const uint32_t mask = (bx == 0 || by == 0) ? 0u : 0xffffffffu;
+      const uint32_t lane_off = (threadIdx.x & 31) * static_cast<uint32_t>(kEntry);
+      v = static_cast<double>(product(smem, bx + by, lane_off, mask, ((cx ^ cy) & 0x80u) << 24));
+    }
+    acc.mac_d(0, v, 1.0);
+  }
+};
+
 // lns16_r11: value = +-2^q * T[f] with log code c = 2048 q + f, T[f] =
 // exp2f(f / 2048) (or exp2 for FP64) from a 2048-entry shared table; the
 // power of two is an exponent-field add, exact because T[f] is in [1, 2) and
@@ -937,12 +1046,27 @@ constexpr int tma_ring(int s, bool fp64) {
 // run a second instantiation with the 64 KiB ring (`Short`). The ring depth
 // stays a compile-time constant: read from the launch parameters instead,
 // it cost the 10-bit codes 14 % (6337 -> 5475 GB/s).
+// A codec may set its own ring (kTmaRing, bytes) and codes per thread per
+// tile (kTmaVpt); 0 keeps the defaults above.
+template <class Codec, class = void> struct tma_overrides {
+  static constexpr int ring = 0, vpt = 0;
+};
+template <class Codec>
+struct tma_overrides<Codec, std::void_t<decltype(Codec::kTmaRing), decltype(Codec::kTmaVpt)>> {
+  static constexpr int ring = Codec::kTmaRing, vpt = Codec::kTmaVpt;
+};
+
+template <class Codec, class Acc, bool Short>
+constexpr int tma_ring_of() {
+  if (tma_overrides<Codec>::ring != 0) return tma_overrides<Codec>::ring;
+  if (Codec::kTableBytes > 1024) return 32 * 1024;
+  return Short ? 64 * 1024 : tma_ring(Codec::kS, std::is_same_v<Acc, acc_f64>);
+}
+
 template <class Codec, class Acc, bool Short = false>
 using tma_shape_of =
-    tma_shape<Codec::kS, ((Codec::kTableBytes > 1024)
-                              ? 32 * 1024
-                              : (Short ? 64 * 1024
-                                       : tma_ring(Codec::kS, std::is_same_v<Acc, acc_f64>)))>;
+    tma_shape<Codec::kS, tma_ring_of<Codec, Acc, Short>(),
+              (tma_overrides<Codec>::vpt != 0 ? tma_overrides<Codec>::vpt : tma_vpt(Codec::kS))>;
 
 // Whether the codec's single-DOT ring is deeper than the batched one.
 template <class Codec, class Acc>
@@ -1140,7 +1264,7 @@ struct kernel_entry {
   kernel_fn fn = nullptr;
   int smem = 0;
   int stride = 0;       // bits per stored slot
-  int table_kind = 0;   // 0 none, 1 lns full f32, 2 lns full f64, 3 frac f32, 4 frac f64
+  int table_kind = 0;   // 0 none, 1/2 full f32/f64, 3/4 frac f32/f64, 5/6 product f32/f64
   uint64_t tile_values = 0;  // codes per block-tile of the vector path
   int blocks_per_sm = 0;
   int runtime = 0;      // rt_codec: dot_params::rt carries the format
@@ -1306,9 +1430,9 @@ int auto_strategy(int32_t format, int32_t layout, int32_t accum) {
 
 // Decoders per format (the reference's decoder_kind axis): the E8 formats,
 // raw storage and e2m3 decode DIRECT (bit moves / hardware conversion);
-// lns8_r3 has FULL_LUT; lns16_r11 has FULL_LUT (FP32 only: the table is
-// 128 KiB of FP32), FRACTION_LUT and FRACTION_LUT_FUSED.  AUTO picks the
-// fastest measured one.
+// lns8_r3 has FULL_LUT and FUSED_SUM_LUT; lns16_r11 has FULL_LUT (FP32
+// only: the table is 128 KiB of FP32), FRACTION_LUT and FRACTION_LUT_FUSED.
+// AUTO picks the fastest measured one.
 kernel_entry lookup(int32_t format, int32_t layout, int32_t accum, int strategy,
                     int decoder = AUT_DECODER_AUTO) {
   using namespace aut::dev;
@@ -1330,7 +1454,10 @@ kernel_entry lookup(int32_t format, int32_t layout, int32_t accum, int strategy,
   if (decoder != AUT_DECODER_AUTO) {
     if (!lns && decoder != AUT_DECODER_DIRECT) return {};
     if (lns && decoder == AUT_DECODER_DIRECT) return {};
-    if (format == AUT_FMT_LNS8_R3 && decoder != AUT_DECODER_FULL_LUT) return {};
+    if (format == AUT_FMT_LNS8_R3 && decoder != AUT_DECODER_FULL_LUT &&
+        decoder != AUT_DECODER_FUSED_SUM_LUT)
+      return {};
+    if (format == AUT_FMT_LNS16_R11 && decoder == AUT_DECODER_FUSED_SUM_LUT) return {};
   }
   if (format == AUT_FMT_LNS16_R11) {
     const bool f32 = accum == AUT_ACCUM_FP32;
@@ -1365,6 +1492,9 @@ kernel_entry lookup(int32_t format, int32_t layout, int32_t accum, int strategy,
   case AUT_FMT_E8M15:
     return dense ? pick<e8_codec<24, 24>>(s, accum, 0) : pick<e8_codec<32, 24>>(s, accum, 0);
   case AUT_FMT_LNS8_R3:
+    if (decoder == AUT_DECODER_FUSED_SUM_LUT)
+      return accum == AUT_ACCUM_FP32 ? make_entry<lns8_fused_codec<float>, acc_f32>(s, 5)
+                                     : make_entry<lns8_fused_codec<double>, acc_f64>(s, 6);
     return accum == AUT_ACCUM_FP32 ? make_entry<lns8_codec<float>, acc_f32>(s, 1)
                                    : make_entry<lns8_codec<double>, acc_f64>(s, 2);
   default: return {};
@@ -1509,6 +1639,8 @@ aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
                   "fraction-table kernels rely on");
     table = e.table_kind == 1   ? static_cast<const void *>(t->full_f32)
             : e.table_kind == 2 ? static_cast<const void *>(t->full_f64)
+            : e.table_kind == 5 ? static_cast<const void *>(t->prod_f32)
+            : e.table_kind == 6 ? static_cast<const void *>(t->prod_f64)
             : e.table_kind == 3 ? static_cast<const void *>(t->frac_f32)
                                 : static_cast<const void *>(t->frac_f64);
   }

@@ -47,6 +47,10 @@ struct code_tables {
   // LNS only:
   float *frac_f32 = nullptr;   // 2^R entries: exp2f(f / 2^R)
   double *frac_f64 = nullptr;  // 2^R entries: exp2(f / 2^R)
+  // B <= 12: entry i = T(exp2((i - 2^(B-1)) / 2^R)), the magnitude of a
+  // product whose two log codes, each biased by 2^(B-2), sum to i
+  float *prod_f32 = nullptr;   // 2^B entries
+  double *prod_f64 = nullptr;  // 2^B entries
   double *thresholds = nullptr; // encode thresholds, 2^(B-1) - 2 entries
   double zero_threshold = 0.0; // smallest magnitude that does not encode to 0
   // +-2^q * frac[f] equals the full decode for every code (FP32 / FP64), so

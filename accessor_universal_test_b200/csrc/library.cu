@@ -303,6 +303,25 @@ aut_status build_code_tables(const format_desc &f, code_tables &t) {
   AUT_CUDA_TRY(cudaMalloc(&t.frac_f32, frac * sizeof(float)));
   AUT_CUDA_TRY(cudaMalloc(&t.frac_f64, frac * sizeof(double)));
   AUT_CUDA_TRY(cudaMalloc(&t.thresholds, thr.size() * sizeof(double)));
+  if (Bb <= 12) {
+    // The fused-sum table (src/lns_strategy_bench.cu:359-374): the product of
+    // two finite codes has a log in [-2 m, 2 m], m = 2^(B-2) - 1; the slots no
+    // product reaches hold the nearest reachable magnitude.
+    const int64_t m = static_cast<int64_t>(aut::detail::lns_special(Bb)) - 1;
+    const int64_t bias = int64_t{1} << (Bb - 1);
+    std::vector<float> prod32(full);
+    std::vector<double> prod64(full);
+    for (size_t i = 0; i < full; ++i) {
+      int64_t lg = static_cast<int64_t>(i) - bias;
+      lg = lg < -2 * m ? -2 * m : (lg > 2 * m ? 2 * m : lg);
+      prod64[i] = std::exp2(static_cast<double>(lg) / scale);
+      prod32[i] = static_cast<float>(prod64[i]);
+    }
+    AUT_CUDA_TRY(cudaMalloc(&t.prod_f32, full * sizeof(float)));
+    AUT_CUDA_TRY(cudaMalloc(&t.prod_f64, full * sizeof(double)));
+    AUT_CUDA_TRY(cudaMemcpy(t.prod_f32, prod32.data(), full * sizeof(float), cudaMemcpyHostToDevice));
+    AUT_CUDA_TRY(cudaMemcpy(t.prod_f64, prod64.data(), full * sizeof(double), cudaMemcpyHostToDevice));
+  }
   AUT_CUDA_TRY(cudaMemcpy(t.full_f32, full32.data(), full * sizeof(float), cudaMemcpyHostToDevice));
   AUT_CUDA_TRY(cudaMemcpy(t.full_f64, full64.data(), full * sizeof(double), cudaMemcpyHostToDevice));
   AUT_CUDA_TRY(cudaMemcpy(t.frac_f32, frac32.data(), frac * sizeof(float), cudaMemcpyHostToDevice));
@@ -317,6 +336,8 @@ void free_code_tables(code_tables &t) {
   cudaFree(t.full_f64);
   cudaFree(t.frac_f32);
   cudaFree(t.frac_f64);
+  cudaFree(t.prod_f32);
+  cudaFree(t.prod_f64);
   cudaFree(t.thresholds);
   t = code_tables{};
 }
@@ -570,7 +591,7 @@ aut_status aut_dot_variant(aut_workspace *ws, int32_t format, int32_t layout,
   if (st != AUT_OK) return st;
   if (strategy < AUT_STRATEGY_AUTO || strategy > AUT_STRATEGY_SCALAR)
     return fail(AUT_ERR_INVALID_ARGUMENT, "unknown access strategy");
-  if (decoder < AUT_DECODER_AUTO || decoder > AUT_DECODER_FRACTION_LUT_FUSED)
+  if (decoder < AUT_DECODER_AUTO || decoder > AUT_DECODER_FUSED_SUM_LUT)
     return fail(AUT_ERR_INVALID_ARGUMENT, "unknown decoder");
   device_scope scope(ws->device);
   AUT_CUDA_TRY(scope.err);
@@ -611,7 +632,7 @@ aut_status aut_gemv(aut_workspace *ws, int32_t format, int32_t layout,
   if (st != AUT_OK) return st;
   if (strategy < AUT_STRATEGY_AUTO || strategy > AUT_STRATEGY_SCALAR)
     return fail(AUT_ERR_INVALID_ARGUMENT, "unknown access strategy");
-  if (decoder < AUT_DECODER_AUTO || decoder > AUT_DECODER_FRACTION_LUT_FUSED)
+  if (decoder < AUT_DECODER_AUTO || decoder > AUT_DECODER_FUSED_SUM_LUT)
     return fail(AUT_ERR_INVALID_ARGUMENT, "unknown decoder");
   if (rows == 0) return AUT_OK;
   if (rows > 0xffffffffull)

@@ -187,7 +187,9 @@ std::vector<decoder_choice> decoders_for(const std::string &fmt, int32_t accum) 
     }
     return {{AUT_DECODER_AUTO, "direct_shift", "ordinary", 0}};  // runtime E/M/bias
   }
-  if (fmt == "lns8_r3") return {{AUT_DECODER_FULL_LUT, "full_lut_shared", "ordinary", 256 * 32 * t}};
+  if (fmt == "lns8_r3")
+    return {{AUT_DECODER_FULL_LUT, "full_lut_shared", "ordinary", 256 * 32 * t},
+            {AUT_DECODER_FUSED_SUM_LUT, "fused_sum_lut_shared", "fused", 256 * 32 * t}};
   if (fmt == "lns16_r11") {
     std::vector<decoder_choice> d;
     if (accum == AUT_ACCUM_FP32)

@@ -405,7 +405,7 @@ def main():
         # every decoder this format/accumulator has, each with both strategies
         table = {}
         for dname, dec in (("direct", 1), ("full_lut", 2), ("fraction_lut", 3),
-                           ("fraction_lut_fused", 4)):
+                           ("fraction_lut_fused", 4), ("fused_sum_lut", 5)):
             for sname, s in (("ldg", 1), ("tma", 2)):
                 try:
                     table[f"{dname}/{sname}"] = packed_bytes[k] / (time_kernel(k, s, dec) / 1e3) / 1e9

@@ -94,8 +94,10 @@ enum {
   AUT_DECODER_DIRECT = 1,      /* bit moves / hardware conversion (E8, e2m3, raw) */
   AUT_DECODER_FULL_LUT = 2,     /* one shared-memory lookup per code (LNS)     */
   AUT_DECODER_FRACTION_LUT = 3, /* fraction table + exponent add (lns16_r11)   */
-  AUT_DECODER_FRACTION_LUT_FUSED = 4 /* logs added, one fraction lookup per
-                                        pair: multiply_kind::fused (lns16_r11) */
+  AUT_DECODER_FRACTION_LUT_FUSED = 4, /* logs added, one fraction lookup per
+                                         pair: multiply_kind::fused (lns16_r11) */
+  AUT_DECODER_FUSED_SUM_LUT = 5 /* logs added, one lookup per pair in a table of
+                                   every product: fused_sum_lut_shared (lns8_r3) */
 };
 
 /* Sticky device status bits reported by aut_workspace_status(). */

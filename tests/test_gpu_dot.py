@@ -37,7 +37,8 @@ def test_dot_matches_oracle(ws, orc, name, layout, strategy):
 
 # (format, accumulator, decoder) triples with a kernel; every other explicit
 # decoder is AUT_ERR_UNSUPPORTED.
-DECODER_CASES = [("lns8_r3", 0, 2), ("lns8_r3", 1, 2), ("lns16_r11", 0, 2),
+DECODER_CASES = [("lns8_r3", 0, 2), ("lns8_r3", 1, 2), ("lns8_r3", 0, 5), ("lns8_r3", 1, 5),
+                 ("lns16_r11", 0, 2),
                  ("lns16_r11", 0, 3), ("lns16_r11", 1, 3), ("lns16_r11", 0, 4),
                  ("lns16_r11", 1, 4), ("e8m5", 0, 1), ("e2m3", 1, 1), ("fp32", 0, 1)]
 
@@ -60,7 +61,7 @@ def test_decoders_without_a_kernel_are_refused(ws):
     res = torch.zeros(1, dtype=torch.float64, device="cuda")
     refused = [("lns16_r11", 1, 2), ("lns16_r11", 0, 1), ("lns8_r3", 0, 3),
                ("lns8_r3", 0, 4), ("lns8_r3", 0, 1), ("e8m0", 0, 2), ("fp32", 0, 3),
-               ("e8m15", 1, 4)]
+               ("e8m15", 1, 4), ("lns16_r11", 0, 5), ("e8m0", 0, 5), ("fp64", 1, 5)]
     for name, accum, decoder in refused:
         with pytest.raises(_lib.AutError) as info:
             ws.dot(_lib.format_id(name), 0, accum, x.data_ptr(), x.data_ptr(), 64,
@@ -68,7 +69,7 @@ def test_decoders_without_a_kernel_are_refused(ws):
         assert info.value.status == _lib.AUT_ERR_UNSUPPORTED, (name, accum, decoder)
     with pytest.raises(_lib.AutError) as info:
         ws.dot(_lib.format_id("e8m0"), 0, 0, x.data_ptr(), x.data_ptr(), 64,
-               res.data_ptr(), decoder=5)
+               res.data_ptr(), decoder=6)
     assert info.value.status == _lib.AUT_ERR_INVALID_ARGUMENT
 
 
@@ -175,7 +176,8 @@ def test_special_codes_propagate_like_the_oracle(ws, orc, name):
                     assert abs(got - want) <= TOL[accum] * s[0], (name, label, pos, got, want)
 
 
-LNS_DECODERS = [("lns8_r3", 0, 2), ("lns8_r3", 1, 2), ("lns16_r11", 0, 2),
+LNS_DECODERS = [("lns8_r3", 0, 2), ("lns8_r3", 1, 2), ("lns8_r3", 0, 5), ("lns8_r3", 1, 5),
+                ("lns16_r11", 0, 2),
                 ("lns16_r11", 0, 3), ("lns16_r11", 1, 3), ("lns16_r11", 0, 4),
                 ("lns16_r11", 1, 4)]
 
