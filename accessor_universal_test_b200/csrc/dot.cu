@@ -573,16 +573,17 @@ struct lns16_full_codec {
 // code is biased by 2^14 (reserved code -> 0, finite codes -> [1, 2^15)), so
 // one 32-bit add sums both halfwords of a word pair without a carry crossing
 // them: halfword h = cx + cy + 2^15, whose low 11 bits index the fraction
-// table and whose top 5 bits are the binary exponent + 16.  The shared copy
-// of the table is pre-scaled by 2^-16, so the exponent is one integer add of
-// (h >> 11) into the exponent field and the product's sign one more add of
-// bit 31.  Products lie in [2^-16, 2^16): always normal, never rounded
-// again.  Reserved codes follow lns::multiply_codes
-// (lns_benchmark_core.hpp:241-254) without branches: adding 0x7fff to a
-// biased halfword sets its top bit exactly when the code is not reserved, a
-// sign-replicating byte permute spreads that bit into a mask that zeroes
-// products with a zero operand, and a reserved code with its sign bit set
-// (NaN) raises a flag that makes the DOT NaN.
+// table and whose top 5 bits are the binary exponent + 16.  The power of two
+// and the product's sign go into the accumulating FMA's second operand,
+// +-2^(top - 16), so acc += T[f] * +-2^q is one FMA of the looked-up entry
+// and the scale: exact, since products lie in [2^-16, 2^16) and are always
+// normal, and the same rounding as adding the exact product.  Reserved codes
+// follow lns::multiply_codes (lns_benchmark_core.hpp:241-254) without
+// branches: adding 0x7fff to a biased halfword sets its top bit exactly when
+// the code is not reserved, a sign-replicating byte permute spreads that bit
+// into a mask that zeroes the scale of products with a zero operand, and a
+// reserved code with its sign bit set (NaN) raises a flag that makes the DOT
+// NaN.
 template <typename T> struct lns16_fused_codec {
   static constexpr int kS = 16;
   static constexpr int kU = 4;
@@ -590,6 +591,7 @@ template <typename T> struct lns16_fused_codec {
   static constexpr int kTableBytes = 2048 * kEntry + 48;  // table + multipliers
   static constexpr bool kExactLanes = false;
   static constexpr int kMant = sizeof(T) == 4 ? 23 : 20;  // exponent shift in the top word
+  static constexpr uint32_t kBias = sizeof(T) == 4 ? 127u : 1023u;
 
   // Field moves done as integer multiplies (x * 2^k for left shifts, the
   // high word of x * 2^k for right shifts, x * 1 + y for adds) run on the
@@ -599,11 +601,11 @@ template <typename T> struct lns16_fused_codec {
   struct multipliers {
     uint32_t one;      // 1
     uint32_t k21;      // 2^21: low fraction (bits 0-10) -> bits 21-31, zeros below
-    uint32_t k5;       // 2^5: high exponent (bits 27-31) -> bits 0-4 (high word)
     uint32_t off;      // 2^(13 + log2 sizeof(T) - 2): bits 21-31 -> byte offset (high word)
     uint32_t off_hi;   // 2^(16 + log2 sizeof(T)): high fraction -> byte offset (high word)
-    uint32_t exp;      // 2^kMant: exponent -> exponent field
-    uint32_t exp_lo;   // 2^(kMant - 11): low exponent (bits 11-15) -> exponent field
+    uint32_t e_lo;     // 2^(kMant - 11): low exponent (bits 11-15) -> exponent field
+    uint32_t e_hi;     // 2^(kMant + 5): high exponent (bits 27-31) -> exponent field (high word)
+    uint32_t e_bias;   // (kBias - 16) << kMant: exponent + 16 -> biased exponent of 2^q
     uint32_t sign_lo;  // 2^16: bit 15 -> bit 31
     uint32_t mag;      // 0x7fff7fff: both log fields
     uint32_t bias;     // 0x40004000: two's complement -> offset binary
@@ -612,26 +614,18 @@ template <typename T> struct lns16_fused_codec {
   static_assert(sizeof(multipliers) == kTableBytes - 2048 * kEntry, "table layout");
 
   __device__ static void prepare(const dot_params &p, unsigned char *smem) {
-    const void *table = p.table;
-    const T *g = static_cast<const T *>(table);
+    const T *g = static_cast<const T *>(p.table);
     T *s = reinterpret_cast<T *>(smem);
-    for (int e = threadIdx.x; e < 2048; e += kThreads) {
-      if constexpr (sizeof(T) == 4) {
-        s[e] = __uint_as_float(__float_as_uint(g[e]) - (16u << kMant));
-      } else {
-        const double t = g[e];
-        s[e] = __hiloint2double(__double2hiint(t) - (16 << kMant), __double2loint(t));
-      }
-    }
+    for (int e = threadIdx.x; e < 2048; e += kThreads) s[e] = g[e];
     if (threadIdx.x == 0) {
       multipliers m{};
       m.one = 1u;
       m.k21 = 1u << 21;
-      m.k5 = 1u << 5;
       m.off = 1u << (kEntry == 4 ? 13 : 14);
       m.off_hi = 1u << (kEntry == 4 ? 18 : 19);
-      m.exp = 1u << kMant;
-      m.exp_lo = 1u << (kMant - 11);
+      m.e_lo = 1u << (kMant - 11);
+      m.e_hi = 1u << (kMant + 5);
+      m.e_bias = (kBias - 16u) << kMant;
       m.sign_lo = 1u << 16;
       m.mag = 0x7fff7fffu;
       m.bias = 0x40004000u;
@@ -646,26 +640,12 @@ template <typename T> struct lns16_fused_codec {
     return r;
   }
 
-  // product from the biased log sum h (bits [0, 16)) and the sign bit at 31
-  __device__ __forceinline__ static T product(uint32_t h, uint32_t sign, const T *tab) {
-    const uint32_t e = (h >> 11) << kMant;
-    if constexpr (sizeof(T) == 4) {
-      return __uint_as_float(__float_as_uint(tab[h & 0x7ffu]) + e + sign);
-    } else {
-      const double t = tab[h & 0x7ffu];
-      return __hiloint2double(static_cast<int>(static_cast<uint32_t>(__double2hiint(t)) + e + sign),
-                              __double2loint(t));
-    }
-  }
-
-  // product() with all bits cleared where the mask is 0 (a zero operand)
-  __device__ __forceinline__ static T masked(T v, uint32_t mask) {
-    if constexpr (sizeof(T) == 4) {
-      return __uint_as_float(__float_as_uint(v) & mask);
-    } else {
-      return __hiloint2double(static_cast<int>(static_cast<uint32_t>(__double2hiint(v)) & mask),
-                              static_cast<int>(static_cast<uint32_t>(__double2loint(v)) & mask));
-    }
+  // +-2^q as T from the top word of its bit pattern
+  __device__ __forceinline__ static T scale_of(uint32_t top) {
+    if constexpr (sizeof(T) == 4)
+      return __uint_as_float(top);
+    else
+      return __hiloint2double(static_cast<int>(top), 0);
   }
 
   // the exact product of two codes, specials included
@@ -677,35 +657,9 @@ template <typename T> struct lns16_fused_codec {
       else return __hiloint2double(0x7ff80000, 0);
     }
     const uint32_t sign = ((cx ^ cy) & 0x8000u) << 16;
-    if (bx == 0 || by == 0) {
-      if constexpr (sizeof(T) == 4) return __uint_as_float(sign);
-      else return __hiloint2double(static_cast<int>(sign), 0);
-    }
-    return product(bx + by, sign, tab);
-  }
-
-  template <class Acc>
-  __device__ __forceinline__ static void add(Acc &acc, int slot, T p) {
-    if constexpr (sizeof(T) == 4)
-      acc.mac(slot, p, 1.0f);
-    else
-      acc.mac_d(slot, p, 1.0);
-  }
-
-  // product of the pair whose biased log sum sits at h's high/low halfword:
-  // table entry at byte offset `off`, exponent field `ef`, live mask, sign
-  __device__ __forceinline__ static T product_at(const unsigned char *smem, uint32_t off,
-                                                 uint32_t ef, uint32_t mask, uint32_t sign,
-                                                 uint32_t one) {
-    if constexpr (sizeof(T) == 4) {
-      const uint32_t q = __float_as_uint(*reinterpret_cast<const float *>(smem + off)) * one + ef;
-      return __uint_as_float((q & mask) | sign);
-    } else {
-      const double t = *reinterpret_cast<const double *>(smem + off);
-      const uint32_t q = static_cast<uint32_t>(__double2hiint(t)) * one + ef;
-      return __hiloint2double(static_cast<int>((q & mask) | sign),
-                              static_cast<int>(static_cast<uint32_t>(__double2loint(t)) & mask));
-    }
+    if (bx == 0 || by == 0) return scale_of(sign);
+    const uint32_t h = bx + by;
+    return tab[h & 0x7ffu] * scale_of((((h >> 11) + kBias - 16u) << kMant) | sign);
   }
 
   template <int NV, class Acc>
@@ -715,7 +669,6 @@ template <typename T> struct lns16_fused_codec {
                                                 const unsigned char *smem) {
     static_assert(NV % 2 == 0, "two codes per word");
     const multipliers m = *reinterpret_cast<const multipliers *>(smem + 2048 * kEntry);
-    constexpr uint32_t kExp = 31u << kMant;   // exponent-field mask
     constexpr uint32_t kOff = 2047u * kEntry;  // byte-offset mask
     uint32_t nan = 0;
 #pragma unroll
@@ -734,18 +687,28 @@ template <typename T> struct lns16_fused_codec {
       // the high fraction has the low exponent below it, so it is masked
       const uint32_t off_lo = __umulhi(h * m.k21, m.off);
       const uint32_t off_hi = __umulhi(h, m.off_hi) & kOff;
-      const uint32_t e_lo = (h * m.exp_lo) & kExp;
-      const uint32_t e_hi = __umulhi(h, m.k5) * m.exp;
+      // biased exponent fields of 2^q (the exponent bits isolated first)
+      const uint32_t e_lo = (h & 0xf800u) * m.e_lo + m.e_bias;
+      const uint32_t e_hi = __umulhi(h & 0xf8000000u, m.e_hi) + m.e_bias;
       const uint32_t s_lo = (sg * m.sign_lo) & 0x80000000u;
       const uint32_t s_hi = sg & 0x80000000u;
-      add(acc, 2 * w, product_at(smem, off_lo, e_lo, spread<1>(live), s_lo, m.one));
-      add(acc, 2 * w + 1, product_at(smem, off_hi, e_hi, spread<3>(live), s_hi, m.one));
+      const T t_lo = *reinterpret_cast<const T *>(smem + off_lo);
+      const T t_hi = *reinterpret_cast<const T *>(smem + off_hi);
+      const T k_lo = scale_of((e_lo & spread<1>(live)) | s_lo);
+      const T k_hi = scale_of((e_hi & spread<3>(live)) | s_hi);
+      if constexpr (sizeof(T) == 4) {
+        acc.mac(2 * w, t_lo, k_lo);
+        acc.mac(2 * w + 1, t_hi, k_hi);
+      } else {
+        acc.mac_d(2 * w, t_lo, k_lo);
+        acc.mac_d(2 * w + 1, t_hi, k_hi);
+      }
     }
     if (nan & 0x80008000u) {
       if constexpr (sizeof(T) == 4)
-        add(acc, 0, __uint_as_float(0x7fc00000u));
+        acc.mac(0, __uint_as_float(0x7fc00000u), 1.0f);
       else
-        add(acc, 0, __hiloint2double(0x7ff80000, 0));
+        acc.mac_d(0, __hiloint2double(0x7ff80000, 0), 1.0);
     }
   }
 
