@@ -730,6 +730,58 @@ template <typename T> struct lns16_fused_codec {
 // of lane l at element e*32 + l) so a warp's lookups are conflict-free -- the
 // reference's full_lut_shared decoder (bitwidth_benchmark_kernels.cuh:166-
 // 288).  S is the slot width: the code width when dense, 8 for padded bytes.
+// Full-table decode of the 9- to 14-bit E8 codes (decode_with_table with
+// full_lut_shared, bitwidth_benchmark_kernels.cuh:166-200): one 32-bit word
+// per code, read from a shared copy of the host table -- the FP32 bit pattern
+// for the FP32 accumulator, the FP64 value's high word (its low word is zero
+// for these codes) for the FP64 accumulator.  The table is not replicated
+// (2^W words, up to 64 KiB), so lanes that look up different codes in one
+// bank wait for each other.
+template <int S, int W, typename T> struct wide_lut_codec {
+  static_assert(W >= 9 && W <= 14, "codes of 9 to 14 bits");
+  static constexpr int kS = S;
+  static constexpr int kU = packet_shape<S>::Q == 1 ? 4 : 1;
+  static constexpr int kTableBytes = (1 << W) * 4;
+  static constexpr bool kExactLanes = false;
+
+  __device__ static void prepare(const dot_params &p, unsigned char *smem) {
+    const uint4 *g = static_cast<const uint4 *>(p.table);
+    uint4 *s = reinterpret_cast<uint4 *>(smem);
+    for (int e = threadIdx.x; e < (1 << W) / 4; e += kThreads) s[e] = g[e];
+  }
+
+  __device__ __forceinline__ static T value(uint32_t code, const unsigned char *smem) {
+    const uint32_t word = reinterpret_cast<const uint32_t *>(smem)[code];
+    if constexpr (sizeof(T) == 4)
+      return __uint_as_float(word);
+    else
+      return __hiloint2double(static_cast<int>(word), 0);
+  }
+
+  template <int NV, class Acc>
+  __device__ __forceinline__ static void values(const uint32_t *xw,
+                                                const uint32_t *yw, Acc &acc,
+                                                float *, const unsigned char *smem) {
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const T a = value(field_low<S, W>(xw, v), smem);
+      const T b = value(field_low<S, W>(yw, v), smem);
+      if constexpr (sizeof(T) == 4)
+        acc.mac(v, a, b);
+      else
+        acc.mac_d(v, a, b);
+    }
+  }
+
+  template <class Acc>
+  __device__ __forceinline__ static void scalar(const unsigned char *xb, uint64_t i,
+                                                const unsigned char *yb, uint64_t j,
+                                                Acc &acc, const unsigned char *smem) {
+    acc.mac_d(0, static_cast<double>(value(load_code<S, W>(xb, i), smem)),
+              static_cast<double>(value(load_code<S, W>(yb, j), smem)));
+  }
+};
+
 template <int S, typename T> struct lut_codec {
   static_assert(S >= 2 && S <= 8, "codes of 2 to 8 bits");
   static constexpr int kS = S;
@@ -1227,7 +1279,8 @@ struct kernel_entry {
   kernel_fn fn = nullptr;
   int smem = 0;
   int stride = 0;       // bits per stored slot
-  int table_kind = 0;   // 0 none, 1/2 full f32/f64, 3/4 frac f32/f64, 5/6 product f32/f64
+  int table_kind = 0;   // 0 none, 1/2 full f32/f64, 3/4 frac f32/f64, 5/6 product f32/f64,
+                        // 7 full FP64 high words
   uint64_t tile_values = 0;  // codes per block-tile of the vector path
   int blocks_per_sm = 0;
   int runtime = 0;      // rt_codec: dot_params::rt carries the format
@@ -1368,6 +1421,13 @@ kernel_entry pick(int strategy, int accum, int table_kind) {
              : make_entry<Codec, aut::dev::acc_f64>(strategy, table_kind);
 }
 
+template <int S, int W>
+kernel_entry wide_pick(int strategy, int accum) {
+  using namespace aut::dev;
+  return accum == AUT_ACCUM_FP32 ? make_entry<wide_lut_codec<S, W, float>, acc_f32>(strategy, 1)
+                                 : make_entry<wide_lut_codec<S, W, double>, acc_f64>(strategy, 7);
+}
+
 // The strategy AUTO resolves to per format and accumulator, chosen from
 // CUDA-event timings of both strategies at N = 2^27 on B200 (packed GB/s,
 // LDG / TMA, FP32 accumulator):
@@ -1414,6 +1474,17 @@ kernel_entry lookup(int32_t format, int32_t layout, int32_t accum, int strategy,
   const bool dense = layout == AUT_LAYOUT_DENSE;
   const int s = strategy;
   const bool lns = format == AUT_FMT_LNS8_R3 || format == AUT_FMT_LNS16_R11;
+  if (decoder == AUT_DECODER_FULL_LUT && !lns) {
+    // the full-table decoder of the bit formats (decode_with_table)
+    switch (format) {
+    case AUT_FMT_E2M3: return lut_lookup(*find_format(format), layout, accum, s);
+    case AUT_FMT_E8M0: return dense ? wide_pick<9, 9>(s, accum) : wide_pick<16, 9>(s, accum);
+    case AUT_FMT_E8M1: return dense ? wide_pick<10, 10>(s, accum) : wide_pick<16, 10>(s, accum);
+    case AUT_FMT_E8M3: return dense ? wide_pick<12, 12>(s, accum) : wide_pick<16, 12>(s, accum);
+    case AUT_FMT_E8M5: return dense ? wide_pick<14, 14>(s, accum) : wide_pick<16, 14>(s, accum);
+    default: return {};
+    }
+  }
   if (decoder != AUT_DECODER_AUTO) {
     if (!lns && decoder != AUT_DECODER_DIRECT) return {};
     if (lns && decoder == AUT_DECODER_DIRECT) return {};
@@ -1600,10 +1671,14 @@ aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
       return fail(AUT_ERR_UNSUPPORTED,
                   "this host's exp2/exp2f break the split LNS decode identity that the "
                   "fraction-table kernels rely on");
+    if ((e.table_kind == 7 && t->full_hi == nullptr) ||
+        ((e.table_kind == 5 || e.table_kind == 6) && t->prod_f32 == nullptr))
+      return fail(AUT_ERR_UNSUPPORTED, "no decode table of this kind for this format");
     table = e.table_kind == 1   ? static_cast<const void *>(t->full_f32)
             : e.table_kind == 2 ? static_cast<const void *>(t->full_f64)
             : e.table_kind == 5 ? static_cast<const void *>(t->prod_f32)
             : e.table_kind == 6 ? static_cast<const void *>(t->prod_f64)
+            : e.table_kind == 7 ? static_cast<const void *>(t->full_hi)
             : e.table_kind == 3 ? static_cast<const void *>(t->frac_f32)
                                 : static_cast<const void *>(t->frac_f64);
   }

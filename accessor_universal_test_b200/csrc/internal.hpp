@@ -44,6 +44,9 @@ struct code_tables {
   int ready = 0;
   float *full_f32 = nullptr;   // 2^B entries
   double *full_f64 = nullptr;  // 2^B entries
+  // bit formats of 9 to 14 bits whose FP64 values all have a zero low word:
+  // the high word per code (the reference's full table for the FP64 target)
+  uint32_t *full_hi = nullptr;  // 2^B entries
   // LNS only:
   float *frac_f32 = nullptr;   // 2^R entries: exp2f(f / 2^R)
   double *frac_f64 = nullptr;  // 2^R entries: exp2(f / 2^R)

@@ -241,18 +241,28 @@ aut_status build_code_tables(const format_desc &f, code_tables &t) {
   if (f.family != AUT_FAMILY_LNS) {
     // bit formats: the full table of every code (FP32: the value narrowed,
     // exact where the format's values are FP32 values)
-    if (Bb > 8) return fail(AUT_ERR_UNSUPPORTED, "decode tables cover bit formats of <= 8 bits");
+    if (Bb > 14) return fail(AUT_ERR_UNSUPPORTED, "decode tables cover bit formats of <= 14 bits");
     const size_t full = size_t{1} << Bb;
     std::vector<float> full32(full);
     std::vector<double> full64(full);
+    std::vector<uint32_t> hi(full);
+    bool low_words_zero = true;
     for (size_t r = 0; r < full; ++r) {
       full64[r] = decode_host(f, static_cast<uint32_t>(r));
       full32[r] = static_cast<float>(full64[r]);
+      uint64_t bits;
+      std::memcpy(&bits, &full64[r], sizeof(bits));
+      hi[r] = static_cast<uint32_t>(bits >> 32);
+      if (static_cast<uint32_t>(bits) != 0u) low_words_zero = false;
     }
     AUT_CUDA_TRY(cudaMalloc(&t.full_f32, full * sizeof(float)));
     AUT_CUDA_TRY(cudaMalloc(&t.full_f64, full * sizeof(double)));
     AUT_CUDA_TRY(cudaMemcpy(t.full_f32, full32.data(), full * sizeof(float), cudaMemcpyHostToDevice));
     AUT_CUDA_TRY(cudaMemcpy(t.full_f64, full64.data(), full * sizeof(double), cudaMemcpyHostToDevice));
+    if (Bb > 8 && low_words_zero) {
+      AUT_CUDA_TRY(cudaMalloc(&t.full_hi, full * sizeof(uint32_t)));
+      AUT_CUDA_TRY(cudaMemcpy(t.full_hi, hi.data(), full * sizeof(uint32_t), cudaMemcpyHostToDevice));
+    }
     t.ready = 1;
     return AUT_OK;
   }
@@ -334,6 +344,7 @@ aut_status build_code_tables(const format_desc &f, code_tables &t) {
 void free_code_tables(code_tables &t) {
   cudaFree(t.full_f32);
   cudaFree(t.full_f64);
+  cudaFree(t.full_hi);
   cudaFree(t.frac_f32);
   cudaFree(t.frac_f64);
   cudaFree(t.prod_f32);
@@ -364,7 +375,7 @@ aut_status code_tables_for(aut_workspace *ws, int32_t format_id,
   if (f == nullptr ||
       !(f->family == AUT_FAMILY_LNS ||
         ((f->family == AUT_FAMILY_BINARY || f->family == AUT_FAMILY_FP64_PREFIX) &&
-         f->total_bits <= 8)))
+         f->total_bits <= 14)))
     return fail(AUT_ERR_INVALID_ARGUMENT, "no decode tables for this format");
   std::lock_guard<std::mutex> lock(ws->mutex);
   int slot = -1;
@@ -513,7 +524,11 @@ aut_status aut_workspace_prepare(aut_workspace *ws, int32_t format) {
   if (ws == nullptr) return fail(AUT_ERR_INVALID_ARGUMENT, "workspace is NULL");
   const format_desc *f = find_format(format);
   if (f == nullptr) return fail(AUT_ERR_INVALID_ARGUMENT, "unknown format id");
-  const bool narrow_bits = format > AUT_FMT_LNS16_R11 && f->total_bits <= 8 &&
+  // bit formats with a table decoder: codes of at most 8 bits, and the E8
+  // codes of 9 to 14 bits (FULL_LUT)
+  const bool wide_e8 = format == AUT_FMT_E8M0 || format == AUT_FMT_E8M1 ||
+                       format == AUT_FMT_E8M3 || format == AUT_FMT_E8M5;
+  const bool narrow_bits = (f->total_bits <= 8 || wide_e8) &&
                            (f->family == AUT_FAMILY_BINARY ||
                             f->family == AUT_FAMILY_FP64_PREFIX);
   if (f->family != AUT_FAMILY_LNS && !narrow_bits) return AUT_OK;

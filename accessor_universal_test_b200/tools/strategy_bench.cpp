@@ -198,7 +198,16 @@ std::vector<decoder_choice> decoders_for(const std::string &fmt, int32_t accum) 
     d.push_back({AUT_DECODER_FRACTION_LUT_FUSED, "fraction_lut_shared", "fused", 2048 * t});
     return d;
   }
-  if (fmt == "e2m3") return {{AUT_DECODER_DIRECT, "native_packed", "ordinary", 0}};
+  if (fmt == "e2m3")
+    return {{AUT_DECODER_DIRECT, "native_packed", "ordinary", 0},
+            {AUT_DECODER_FULL_LUT, "full_lut_shared", "ordinary", 64 * 32 * t}};
+  if (fmt == "e8m0" || fmt == "e8m1" || fmt == "e8m3" || fmt == "e8m5") {
+    const int32_t fid = aut_format_id(fmt.c_str());
+    int32_t family = 0, bits = 0, e = 0, fin = 0;
+    aut_format_info(fid, &family, &bits, &e, &fin);
+    return {{AUT_DECODER_DIRECT, "direct_shift", "ordinary", 0},
+            {AUT_DECODER_FULL_LUT, "full_lut_shared", "ordinary", (1 << bits) * 4}};
+  }
   return {{AUT_DECODER_DIRECT, "direct_shift", "ordinary", 0}};
 }
 

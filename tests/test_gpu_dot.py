@@ -40,7 +40,9 @@ def test_dot_matches_oracle(ws, orc, name, layout, strategy):
 DECODER_CASES = [("lns8_r3", 0, 2), ("lns8_r3", 1, 2), ("lns8_r3", 0, 5), ("lns8_r3", 1, 5),
                  ("lns16_r11", 0, 2),
                  ("lns16_r11", 0, 3), ("lns16_r11", 1, 3), ("lns16_r11", 0, 4),
-                 ("lns16_r11", 1, 4), ("e8m5", 0, 1), ("e2m3", 1, 1), ("fp32", 0, 1)]
+                 ("lns16_r11", 1, 4), ("e8m5", 0, 1), ("e2m3", 1, 1), ("fp32", 0, 1),
+                 ("e2m3", 0, 2), ("e2m3", 1, 2), ("e8m0", 0, 2), ("e8m0", 1, 2),
+                 ("e8m1", 0, 2), ("e8m3", 1, 2), ("e8m5", 0, 2), ("e8m5", 1, 2)]
 
 
 @pytest.mark.parametrize("name,accum,decoder", DECODER_CASES)
@@ -54,13 +56,32 @@ def test_every_decoder_matches_oracle(ws, orc, name, accum, decoder, strategy):
         assert err <= TOL[accum], (name, accum, decoder, n, got, float(ref_dot), float(err))
 
 
+@pytest.mark.parametrize("name", ["e2m3", "e8m0", "e8m1", "e8m3", "e8m5"])
+@pytest.mark.parametrize("layout", [0, 1])
+@pytest.mark.parametrize("strategy", [1, 2])
+def test_full_table_decoder_equals_direct_decode(ws, orc, name, layout, strategy):
+    """FULL_LUT (decode_with_table, one table word per code) against the
+    oracle in both layouts; the e2m3 DOT is exact up to its final rounding
+    with either decoder, so the two decoders agree bit for bit there."""
+    for n in (5, 4099, (1 << 20) + 37):
+        x, y = device_pair(ws, name, layout, n)
+        ref_dot, ref_abs = oracle_dot(orc, name, n)
+        for accum in (0, 1):
+            got = gpu_dot(ws, name, layout, accum, x, y, n, strategy=strategy, decoder=2)
+            err = normalized_error(got, ref_dot, ref_abs)
+            assert err <= TOL[accum], (name, layout, accum, n, got, float(ref_dot), float(err))
+            if name == "e2m3":
+                assert got == float(ref_dot), (name, layout, accum, n, got, float(ref_dot))
+
+
 def test_decoders_without_a_kernel_are_refused(ws):
     import torch
     from accessor_universal_test_b200 import _lib
     x = torch.zeros(4096, dtype=torch.uint8, device="cuda")
     res = torch.zeros(1, dtype=torch.float64, device="cuda")
     refused = [("lns16_r11", 1, 2), ("lns16_r11", 0, 1), ("lns8_r3", 0, 3),
-               ("lns8_r3", 0, 4), ("lns8_r3", 0, 1), ("e8m0", 0, 2), ("fp32", 0, 3),
+               ("lns8_r3", 0, 4), ("lns8_r3", 0, 1), ("e8m15", 0, 2), ("bf16_e8m7", 1, 2),
+               ("fp32", 0, 2), ("e8m0", 0, 3), ("fp32", 0, 3),
                ("e8m15", 1, 4), ("lns16_r11", 0, 5), ("e8m0", 0, 5), ("fp64", 1, 5)]
     for name, accum, decoder in refused:
         with pytest.raises(_lib.AutError) as info:
