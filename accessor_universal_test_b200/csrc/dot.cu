@@ -83,6 +83,7 @@ template <int S, int W> struct e8_codec {
   // not finite is redone with both operands widened: the result is the same
   // FP64 sum of exact products either way.
   static constexpr bool kProductWidening = W - 9 <= 11;
+  static constexpr int kW = W;
 
   template <int NV, class Acc>
   __device__ __forceinline__ static void values(const uint32_t *xw,
@@ -1265,6 +1266,200 @@ __global__ void __launch_bounds__(kThreads)
               p.tickets + batch, p.results + batch, scratch);
 }
 
+
+// ---------------------------------------------------------------------------
+// GEMV with the vector decoded once per block (FP32 accumulation, E8 codes
+// and raw FP32).  Block (s, b) owns column segment s -- one tile of the DOT
+// kernels' shape, so one bulk copy per row -- and the contiguous rows of
+// groups [b * groups_per_block, (b + 1) * groups_per_block).  It decodes its
+// vector segment into registers once, streams its rows' tiles through the
+// bulk-copy ring, and multiplies each row tile by the register-resident
+// vector: one decode per matrix element instead of two.  Every thread's row
+// partial (two FP32 chains of at most 32 products, summed in FP64) is staged
+// in shared memory; after each group of eight rows one warp per row sums its
+// 256 partials in a fixed order into the row's segment partial; a second
+// kernel sums each row's segment partials in segment order, so results do
+// not depend on scheduling (and the streaming kernel issues no fences or
+// atomics).
+// ---------------------------------------------------------------------------
+struct gemv_params {
+  const unsigned char *matrix;  // row r at matrix + r * row_bytes
+  const unsigned char *vector;
+  uint64_t row_bytes;
+  uint32_t rows;               // rows of this launch
+  uint32_t groups_per_block;   // groups of kGemvRows rows
+  double *partials;            // [rows][gridDim.x]
+  unsigned int *status;
+};
+
+constexpr int kGemvRows = kThreads / 32;  // rows per group: one warp per row
+
+// One operand per stage (tma_shape's ring counts two, so the ring is half the
+// figure).  From a sweep of 64-256 on B200 (1024 x 2^17, FP32, GB/s at 96 /
+// 128 / 192): 9-bit codes 4123 / 4324 / 4087 take 128, the others 96 (e8m1
+// 4547 / 3897 / 3900, e8m5 5481 / 5326 / 5208, e8m15 6243 / 6242 / 5989):
+// the 16 KiB row staging beside a bigger ring costs a block per SM.
+constexpr int gemv_ring(int s) { return (s == 9 ? 128 : 96) * 1024; }
+
+template <class Codec>
+using gemv_shape = tma_shape<Codec::kS, gemv_ring(Codec::kS),
+                             (tma_vpt(Codec::kS) > 32 ? tma_vpt(Codec::kS) : 32)>;
+
+__device__ __forceinline__ void gemv_publish(const gemv_params &g, uint32_t r, double v) {
+  g.partials[static_cast<uint64_t>(r) * gridDim.x + blockIdx.x] = v;
+}
+
+// results[r] = the sum of row r's segment partials: one warp per row, lane l
+// taking segments l, l + 32, ... in order, then the warp's fixed tree.
+__global__ void __launch_bounds__(kThreads)
+    gemv_rows_kernel(const double *partials, uint32_t segments, uint32_t rows,
+                     double *results) {
+  const uint32_t r = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
+  const uint32_t lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const double *row = partials + static_cast<uint64_t>(r) * segments;
+  double s = 0.0;
+  for (uint32_t j = lane; j < segments; j += 32) s += row[j];
+  s = warp_sum(s);
+  if (lane == 0) results[r] = s;
+}
+
+template <class Codec>
+__global__ void __launch_bounds__(kThreads)
+    gemv_tma_kernel(const gemv_params g) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  using shape = gemv_shape<Codec>;
+  constexpr int S = Codec::kS;
+  constexpr int W = Codec::kW;
+  constexpr int UV = shape::UV;
+  constexpr int V = shape::V;
+  constexpr int GROUP = shape::GROUP;
+  constexpr int LW = shape::LW;
+  constexpr int VPT = shape::VPT;
+  constexpr int STAGES = shape::STAGES;
+  constexpr int TILE_BYTES = shape::TILE_BYTES;
+  static_assert(VPT <= 64, "two chains of at most 32 products per row tile");
+  __shared__ __align__(8) uint64_t full[STAGES];
+  unsigned char *ring = smem;
+  double *red = reinterpret_cast<double *>(smem + STAGES * TILE_BYTES);  // [kGemvRows][kThreads]
+
+  const uint32_t first_row = blockIdx.y * g.groups_per_block * kGemvRows;
+  const uint32_t end_row = min(g.rows, first_row + g.groups_per_block * kGemvRows);
+  const uint32_t tiles = end_row > first_row ? end_row - first_row : 0;
+  const unsigned char *seg = g.matrix + static_cast<uint64_t>(blockIdx.x) * TILE_BYTES;
+
+  auto issue = [&](uint32_t t, uint32_t stage) {
+    uint64_t *bar = &full[stage];
+    mbar_expect_tx(bar, TILE_BYTES);
+    bulk_load(ring + stage * TILE_BYTES, seg + static_cast<uint64_t>(first_row + t) * g.row_bytes,
+              TILE_BYTES, bar);
+  };
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (uint32_t t = 0; t < tiles && t < static_cast<uint32_t>(STAGES); ++t) issue(t, t);
+
+  // this thread's codes of the vector segment, decoded once
+  float vec[VPT];
+  {
+    const uint32_t *vw = reinterpret_cast<const uint32_t *>(
+        g.vector + static_cast<uint64_t>(blockIdx.x) * TILE_BYTES);
+#pragma unroll
+    for (int v = 0; v < V / GROUP; ++v) {
+      const int u = threadIdx.x + v * kThreads;
+      uint32_t w[LW];
+#pragma unroll
+      for (int q = 0; q < LW; ++q) w[q] = __ldg(vw + u * LW + q);
+#pragma unroll
+      for (int i = 0; i < UV * GROUP; ++i)
+        vec[v * UV * GROUP + i] = __uint_as_float(field_top<S, W>(w, i));
+    }
+  }
+
+  bool failed = false;
+  uint32_t stage = 0, phase = 0, k = 0, done = 0;  // done: rows finished
+  for (uint32_t t = 0; t < tiles; ++t) {
+    const bool ok = mbar_wait(&full[stage], phase);
+    const uint32_t *ws = reinterpret_cast<const uint32_t *>(ring + stage * TILE_BYTES);
+    float c0 = 0.f, c1 = 0.f;
+#pragma unroll
+    for (int v = 0; v < V / GROUP; ++v) {
+      const int u = threadIdx.x + v * kThreads;
+      uint32_t w[LW];
+      if constexpr (LW % 4 == 0) {
+#pragma unroll
+        for (int q = 0; q < LW / 4; ++q) {
+          const uint4 a = reinterpret_cast<const uint4 *>(ws)[u * (LW / 4) + q];
+          w[4 * q] = a.x; w[4 * q + 1] = a.y; w[4 * q + 2] = a.z; w[4 * q + 3] = a.w;
+        }
+      } else if constexpr (LW % 2 == 0) {
+#pragma unroll
+        for (int q = 0; q < LW / 2; ++q) {
+          const uint2 a = reinterpret_cast<const uint2 *>(ws)[u * (LW / 2) + q];
+          w[2 * q] = a.x; w[2 * q + 1] = a.y;
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < LW; ++q) w[q] = ws[u * LW + q];
+      }
+#pragma unroll
+      for (int i = 0; i < UV * GROUP; ++i) {
+        const float m = __uint_as_float(field_top<S, W>(w, i));
+        if (i & 1)
+          c1 = fmaf(m, vec[v * UV * GROUP + i], c1);
+        else
+          c0 = fmaf(m, vec[v * UV * GROUP + i], c0);
+      }
+    }
+    red[k * kThreads + threadIdx.x] = static_cast<double>(c0) + static_cast<double>(c1);
+    // every thread is done with this stage, and red[k] is complete, before
+    // the stage is refilled or the group reduced
+    if (__syncthreads_or(ok ? 0 : 1)) {
+      failed = true;
+      break;
+    }
+    if (threadIdx.x == 0 && t + STAGES < tiles) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue(t + STAGES, stage);
+    }
+    if (++stage == static_cast<uint32_t>(STAGES)) {
+      stage = 0;
+      phase ^= 1u;
+    }
+    if (++k == static_cast<uint32_t>(kGemvRows) || t + 1 == tiles) {
+      // one warp per row of the group: 8 partials per lane, then the warp
+      const uint32_t row = threadIdx.x >> 5, lane = threadIdx.x & 31;
+      if (row < k) {
+        const double *p = red + row * kThreads + lane * 8;
+        double s = 0.0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s += p[j];
+        s = warp_sum(s);
+        if (lane == 0) gemv_publish(g, first_row + done + row, s);
+      }
+      done += k;
+      k = 0;
+      __syncthreads();  // red is read before the next group writes it
+    }
+  }
+  if (failed) {
+    // Let the copies still in flight land, then give every unfinished row of
+    // this block a NaN partial.
+    if (threadIdx.x == 0) {
+      const uint32_t t0 = done + k;
+      for (uint32_t j = t0; j < tiles && j < t0 + STAGES; ++j)
+        mbar_wait(&full[j % STAGES], (j / STAGES) & 1u);
+      atomicOr(g.status, static_cast<unsigned int>(AUT_STATUS_WAIT_TIMEOUT));
+    }
+    __syncthreads();
+    for (uint32_t r = done + threadIdx.x; r < tiles; r += kThreads)
+      gemv_publish(g, first_row + r, __longlong_as_double(0x7ff8000000000000ll));
+  }
+}
+
 } // namespace aut::dev
 
 // ---------------------------------------------------------------------------
@@ -1707,6 +1902,123 @@ aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
     e.fn<<<grid, aut::dev::kThreads, e.smem, static_cast<cudaStream_t>(stream)>>>(p);
     AUT_CUDA_TRY(cudaGetLastError());
   }
+  return AUT_OK;
+}
+
+// ---- GEMV with the vector decoded once per block ----------------------------
+struct gemv_entry {
+  void (*fn)(aut::dev::gemv_params) = nullptr;
+  int smem = 0;
+  uint64_t tile_values = 0;
+  uint64_t tile_bytes = 0;
+};
+
+template <class Codec>
+gemv_entry make_gemv_entry() {
+  using shape = aut::dev::gemv_shape<Codec>;
+  gemv_entry e;
+  e.fn = aut::dev::gemv_tma_kernel<Codec>;
+  e.smem = shape::STAGES * shape::TILE_BYTES + aut::dev::kGemvRows * aut::dev::kThreads * 8;
+  e.tile_values = shape::TILE_VALUES;
+  e.tile_bytes = shape::TILE_BYTES;
+  return e;
+}
+
+static gemv_entry gemv_lookup(int32_t format, int32_t layout) {
+  using namespace aut::dev;
+  const bool dense = layout == AUT_LAYOUT_DENSE;
+  switch (format) {
+  case AUT_FMT_FP32: return make_gemv_entry<e8_codec<32, 32>>();
+  case AUT_FMT_E8M0: return dense ? make_gemv_entry<e8_codec<9, 9>>() : make_gemv_entry<e8_codec<16, 9>>();
+  case AUT_FMT_E8M1: return dense ? make_gemv_entry<e8_codec<10, 10>>() : make_gemv_entry<e8_codec<16, 10>>();
+  case AUT_FMT_E8M3: return dense ? make_gemv_entry<e8_codec<12, 12>>() : make_gemv_entry<e8_codec<16, 12>>();
+  case AUT_FMT_E8M5: return dense ? make_gemv_entry<e8_codec<14, 14>>() : make_gemv_entry<e8_codec<16, 14>>();
+  case AUT_FMT_BF16_E8M7: return make_gemv_entry<e8_codec<16, 16>>();
+  case AUT_FMT_E8M15: return dense ? make_gemv_entry<e8_codec<24, 24>>() : make_gemv_entry<e8_codec<32, 24>>();
+  default: return {};
+  }
+}
+
+static aut_status gemv_blocks_per_sm(const gemv_entry &e, int *out) {
+  static std::mutex mutex;
+  static void (*fns[64])(aut::dev::gemv_params) = {};
+  static int blocks[64] = {};
+  static int count = 0;
+  std::lock_guard<std::mutex> lock(mutex);
+  for (int k = 0; k < count; ++k)
+    if (fns[k] == e.fn) {
+      *out = blocks[k];
+      return AUT_OK;
+    }
+  AUT_CUDA_TRY(cudaFuncSetAttribute(reinterpret_cast<const void *>(e.fn),
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, e.smem));
+  int b = 0;
+  AUT_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+      &b, reinterpret_cast<const void *>(e.fn), aut::dev::kThreads, e.smem));
+  if (b < 1) return fail(AUT_ERR_UNSUPPORTED, "GEMV kernel does not fit on an SM");
+  if (count < 64) {
+    fns[count] = e.fn;
+    blocks[count] = b;
+    ++count;
+  }
+  *out = b;
+  return AUT_OK;
+}
+
+// The GEMV path that decodes the vector once per block: FP32 accumulation,
+// the E8 codes and raw FP32, decoder AUTO/DIRECT, strategy AUTO/TMA, whole
+// segments (columns a multiple of one tile) and 16-byte aligned operands.
+// *handled is false when the call does not qualify; aut_gemv then runs the
+// rows as a batch of DOTs.
+aut_status gemv_launch(aut_workspace *ws, int32_t format, int32_t layout, int32_t accum,
+                       int32_t strategy, int32_t decoder, const void *matrix,
+                       const void *vector, uint64_t rows, uint64_t columns,
+                       double *results, void *stream, bool *handled) {
+  *handled = false;
+  if (accum != AUT_ACCUM_FP32) return AUT_OK;
+  if (strategy != AUT_STRATEGY_AUTO && strategy != AUT_STRATEGY_TMA) return AUT_OK;
+  if (decoder != AUT_DECODER_AUTO && decoder != AUT_DECODER_DIRECT) return AUT_OK;
+  const gemv_entry e = gemv_lookup(format, layout);
+  if (e.fn == nullptr || columns == 0 || rows == 0 || columns % e.tile_values != 0) return AUT_OK;
+  if ((reinterpret_cast<uintptr_t>(matrix) | reinterpret_cast<uintptr_t>(vector)) & 15u)
+    return AUT_OK;
+  const uint64_t segments = columns / e.tile_values;
+  if (segments > static_cast<uint64_t>(ws->max_blocks) || segments > 65535u) return AUT_OK;
+  int per_sm = 0;
+  aut_status st = gemv_blocks_per_sm(e, &per_sm);
+  if (st != AUT_OK) return st;
+  const uint64_t row_bytes = segments * e.tile_bytes;
+  const uint64_t cap = static_cast<uint64_t>(ws->sm_count) * per_sm;
+  const uint64_t group_rows = aut::dev::kGemvRows;
+  for (uint64_t r0 = 0; r0 < rows; r0 += kMaxBatchPerLaunch) {
+    const uint64_t rc = rows - r0 < static_cast<uint64_t>(kMaxBatchPerLaunch)
+                            ? rows - r0
+                            : static_cast<uint64_t>(kMaxBatchPerLaunch);
+    // about one block per resident slot: each block takes an equal run of
+    // row groups for its segment
+    const uint64_t groups = (rc + group_rows - 1) / group_rows;
+    uint64_t per_segment = cap / segments;
+    if (per_segment < 1) per_segment = 1;
+    const uint64_t groups_per_block = (groups + per_segment - 1) / per_segment;
+    const uint64_t blocks_y = (groups + groups_per_block - 1) / groups_per_block;
+    aut::dev::gemv_params g{};
+    g.matrix = static_cast<const unsigned char *>(matrix) + r0 * row_bytes;
+    g.vector = static_cast<const unsigned char *>(vector);
+    g.row_bytes = row_bytes;
+    g.rows = static_cast<uint32_t>(rc);
+    g.groups_per_block = static_cast<uint32_t>(groups_per_block);
+    g.partials = ws->partials;
+    g.status = ws->tickets + kMaxBatchPerLaunch;
+    dim3 grid(static_cast<unsigned>(segments), static_cast<unsigned>(blocks_y));
+    e.fn<<<grid, aut::dev::kThreads, e.smem, static_cast<cudaStream_t>(stream)>>>(g);
+    AUT_CUDA_TRY(cudaGetLastError());
+    constexpr uint64_t rows_per_block = aut::dev::kThreads / 32;
+    aut::dev::gemv_rows_kernel<<<static_cast<unsigned>((rc + rows_per_block - 1) / rows_per_block),
+                                 aut::dev::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        ws->partials, static_cast<uint32_t>(segments), static_cast<uint32_t>(rc), results + r0);
+    AUT_CUDA_TRY(cudaGetLastError());
+  }
+  *handled = true;
   return AUT_OK;
 }
 

@@ -13,6 +13,10 @@
 
 namespace aut::lib {
 
+aut_status gemv_launch(aut_workspace *ws, int32_t format, int32_t layout, int32_t accum,
+                       int32_t strategy, int32_t decoder, const void *matrix,
+                       const void *vector, uint64_t rows, uint64_t columns,
+                       double *results, void *stream, bool *handled);
 aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
                       int32_t accum, int32_t strategy, int32_t decoder,
                       const void *x, const void *y, uint64_t n, uint32_t batch,
@@ -666,6 +670,10 @@ aut_status aut_gemv(aut_workspace *ws, int32_t format, int32_t layout,
     bl.x_index_stride = columns;
   device_scope scope(ws->device);
   AUT_CUDA_TRY(scope.err);
+  bool handled = false;
+  st = gemv_launch(ws, format, layout, accum, strategy, decoder, matrix, vector, rows,
+                   columns, result, stream, &handled);
+  if (st != AUT_OK || handled) return st;
   return dot_launch(ws, format, layout, accum, strategy, decoder, matrix, vector,
                     columns, static_cast<uint32_t>(rows), bl, result, stream,
                     ws->partials, ws->tickets, ws->tickets + kMaxBatchPerLaunch,

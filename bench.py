@@ -416,7 +416,11 @@ def main():
         raise RuntimeError("a bounded device wait timed out during the benchmark")
     peak, peak_kind = measured_peak()
     dom = max(per_kernel, key=lambda r: r[1])
-    traffic = committed_traffic().get(dom[0])
+    # an FP32 GEMV of these formats whose columns are whole 16384-value
+    # segments runs two kernels (the streaming kernel and the row sums)
+    launches_per_call = (2 if gemv and accum == _lib.ACC_FP32 and args.strategy != "ldg"
+                         and cols % 16384 == 0 else 1)
+    traffic = committed_traffic().get(f"gemv:{dom[0]}" if gemv else dom[0])
     if traffic is not None and "bytes_per_value_pair" in traffic:
         traffic = traffic["bytes_per_value_pair"] * n
     elif traffic is not None:
@@ -512,7 +516,7 @@ def main():
         "cpu_baseline": cpu_baseline,
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": 8 * len(fmts) * rows},
-        "gpu_launches": len(fmts) * args.steps,
+        "gpu_launches": len(fmts) * args.steps * launches_per_call,
         "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"],
                    "reasons": clk["reasons"]},
     }

@@ -120,3 +120,65 @@ def test_gemv_degenerate_shapes(ws):
     with pytest.raises(_lib.AutError) as info:
         ws.gemv(fid, 0, 0, buf.data_ptr(), buf.data_ptr(), 1 << 33, 4, out.data_ptr())
     assert info.value.status == _lib.AUT_ERR_TOO_LARGE
+
+
+# The FP32 GEMV of the E8 codes and raw FP32 decodes the vector once per block
+# when the columns are whole segments (one bulk-copy tile per row: 16384
+# values for 9-bit codes, 8192 for the others).
+VECTOR_ONCE = ["e8m0", "e8m1", "e8m3", "e8m5", "bf16_e8m7", "e8m15", "fp32"]
+
+
+@pytest.mark.parametrize("name", VECTOR_ONCE)
+@pytest.mark.parametrize("layout", [0, 1])
+def test_gemv_vector_once_rows_match_oracle(ws, orc, name, layout):
+    # 1 row; 37 rows (a ragged group of 5); 1030 rows (two launches)
+    for rows, columns in ((1, 16384), (37, 32768), (1030, 16384)):
+        if name == "fp32" and layout == 1:
+            continue
+        m, v, ref = _operands(ws, orc, name, layout, rows, columns)
+        got = _gemv(ws, name, layout, 0, m, v, rows, columns)
+        _check_rows(got, ref, 0, rows, (name, layout, rows, columns))
+
+
+def test_gemv_vector_once_is_deterministic(ws, orc):
+    rows, columns = 300, 1 << 16
+    m, v, _ = _operands(ws, orc, "e8m3", 0, rows, columns)
+    a = _gemv(ws, "e8m3", 0, 0, m, v, rows, columns)
+    for _ in range(3):
+        b = _gemv(ws, "e8m3", 0, 0, m, v, rows, columns)
+        assert a.tobytes() == b.tobytes()
+
+
+def test_gemv_vector_once_special_values(ws, orc):
+    """Inf and NaN codes in the matrix and the vector reach the rows they
+    touch, and only those."""
+    import torch
+    from accessor_universal_test_b200 import _lib
+    rows, columns = 24, 16384
+    desc = _lib.format_info(_lib.format_id("e8m5"))
+    vals = orc.synthetic(0, 5, 0, rows * columns).reshape(rows, columns)
+    vec = orc.synthetic(0, 5, 1, columns)
+    vals[3, 100] = np.inf
+    vals[7, 9000] = np.nan
+    vals[11, 5] = np.inf
+    vals[11, 6] = -np.inf
+    mc = orc.encode(desc, vals.ravel())
+    vc = orc.encode(desc, vec)
+    fid = _lib.format_id("e8m5")
+    bufs = []
+    for codes in (mc, vc):
+        words = orc.pack_dense(desc[1], codes)
+        assert words.size * 4 == _lib.storage_bytes(fid, 0, codes.size)
+        bufs.append(torch.from_numpy(words.view(np.uint8).copy()).cuda())
+    got = _gemv(ws, "e8m5", 0, 0, bufs[0], bufs[1], rows, columns)
+    dec_m = orc.decode_f64(desc, mc).reshape(rows, columns)
+    dec_v = orc.decode_f64(desc, vc)
+    for r in range(rows):
+        with np.errstate(invalid="ignore", over="ignore"):
+            want = float((dec_m[r] * dec_v).sum())
+        if np.isnan(want):
+            assert np.isnan(got[r]), r
+        elif np.isinf(want):
+            assert got[r] == want, (r, got[r], want)
+        else:
+            assert np.isfinite(got[r]), r
