@@ -423,6 +423,9 @@ def main():
     traffic = committed_traffic().get(f"gemv:{dom[0]}" if gemv else dom[0])
     if traffic is not None and "bytes_per_value_pair" in traffic:
         traffic = traffic["bytes_per_value_pair"] * n
+    elif traffic is not None and "captured_columns" in traffic:  # GEMV, scaled to this shape
+        cr, cc = traffic["captured_rows"], traffic["captured_columns"]
+        traffic = traffic["bytes_per_launch"] * (rows * cols + cols) / (cr * cc + cc)
     elif traffic is not None:
         traffic = traffic.get("bytes_per_launch")
 
