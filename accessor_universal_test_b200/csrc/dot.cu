@@ -1294,12 +1294,34 @@ struct gemv_params {
 
 constexpr int kGemvRows = kThreads / 32;  // rows per group: one warp per row
 
+// c + a * b for two bf16 values, exact product, one rounding (the sm_100
+// mixed-precision FMA): `a_top` holds a in its high half (FP32 bits whose low
+// half is zero), `pair` holds b in its low (H = false) or high (H = true) half.
+template <bool H>
+__device__ __forceinline__ float fma_bf16(uint32_t a_top, uint32_t pair, float c) {
+  if constexpr (H)
+    asm("{\n\t.reg .b16 al, ah, bl, bh;\n\t"
+        "mov.b32 {al, ah}, %1;\n\t"
+        "mov.b32 {bl, bh}, %2;\n\t"
+        "fma.rn.f32.bf16 %0, ah, bh, %0;\n\t}"
+        : "+f"(c)
+        : "r"(a_top), "r"(pair));
+  else
+    asm("{\n\t.reg .b16 al, ah, bl, bh;\n\t"
+        "mov.b32 {al, ah}, %1;\n\t"
+        "mov.b32 {bl, bh}, %2;\n\t"
+        "fma.rn.f32.bf16 %0, ah, bl, %0;\n\t}"
+        : "+f"(c)
+        : "r"(a_top), "r"(pair));
+  return c;
+}
+
 // One operand per stage (tma_shape's ring counts two, so the ring is half the
-// figure).  From a sweep of 64-256 on B200 (1024 x 2^17, FP32, GB/s at 96 /
-// 128 / 192): 9-bit codes 4123 / 4324 / 4087 take 128, the others 96 (e8m1
-// 4547 / 3897 / 3900, e8m5 5481 / 5326 / 5208, e8m15 6243 / 6242 / 5989):
-// the 16 KiB row staging beside a bigger ring costs a block per SM.
-constexpr int gemv_ring(int s) { return (s == 9 ? 128 : 96) * 1024; }
+// figure).  From sweeps of 64-256 on B200 (1024 x 2^17, FP32, GB/s at 96 /
+// 128): e8m0 4590 / 4322, e8m1 5107 / 4480, e8m3 5408 / 5224, e8m5 5651 /
+// 5477, bf16 5829 / 5934, e8m15 6284 / 6282: beside the 16 KiB row staging a
+// bigger ring costs a block per SM, except for 16-bit codes.
+constexpr int gemv_ring(int s) { return (s == 16 ? 128 : 96) * 1024; }
 
 template <class Codec>
 using gemv_shape = tma_shape<Codec::kS, gemv_ring(Codec::kS),
@@ -1365,8 +1387,12 @@ __global__ void __launch_bounds__(kThreads, Codec::kS == 12 ? 3 : 1)
   if (threadIdx.x == 0)
     for (uint32_t t = 0; t < tiles && t < static_cast<uint32_t>(STAGES); ++t) issue(t, t);
 
-  // this thread's codes of the vector segment, decoded once
-  float vec[VPT];
+  // this thread's codes of the vector segment, decoded once: codes of up to
+  // 16 bits are bf16 values exactly and are kept as bf16 pairs (half the
+  // registers, so more blocks fit an SM); wider ones as FP32
+  constexpr bool kPairs = W <= 16;
+  float vec[kPairs ? 1 : VPT];
+  uint32_t vec2[kPairs ? VPT / 2 : 1];
   {
     const uint32_t *vw = reinterpret_cast<const uint32_t *>(
         g.vector + static_cast<uint64_t>(blockIdx.x) * TILE_BYTES);
@@ -1377,69 +1403,107 @@ __global__ void __launch_bounds__(kThreads, Codec::kS == 12 ? 3 : 1)
 #pragma unroll
       for (int q = 0; q < LW; ++q) w[q] = __ldg(vw + u * LW + q);
 #pragma unroll
-      for (int i = 0; i < UV * GROUP; ++i)
-        vec[v * UV * GROUP + i] = __uint_as_float(field_top<S, W>(w, i));
+      for (int i = 0; i < UV * GROUP; ++i) {
+        const uint32_t bits = field_top<S, W>(w, i);
+        const int j = v * UV * GROUP + i;
+        if constexpr (kPairs) {
+          if (j & 1)
+            vec2[j >> 1] = __byte_perm(vec2[j >> 1], bits, 0x7610);
+          else
+            vec2[j >> 1] = bits >> 16;
+        } else {
+          vec[j] = __uint_as_float(bits);
+        }
+      }
     }
   }
 
+  // Rings of four or more stages consume two row tiles per block barrier.
+  constexpr uint32_t kPerSync = STAGES >= 4 ? 2 : 1;
   bool failed = false;
   uint32_t stage = 0, phase = 0, k = 0, done = 0;  // done: rows finished
-  for (uint32_t t = 0; t < tiles; ++t) {
-    const bool ok = mbar_wait(&full[stage], phase);
-    const uint32_t *ws = reinterpret_cast<const uint32_t *>(ring + stage * TILE_BYTES);
-    float c0 = 0.f, c1 = 0.f;
+  for (uint32_t t = 0; t < tiles; t += kPerSync) {
+    const uint32_t n = tiles - t < kPerSync ? tiles - t : kPerSync;  // same in every thread
+    bool ok = true;
 #pragma unroll
-    for (int v = 0; v < V / GROUP; ++v) {
-      const int u = threadIdx.x + v * kThreads;
-      uint32_t w[LW];
-      if constexpr (LW % 4 == 0) {
-#pragma unroll
-        for (int q = 0; q < LW / 4; ++q) {
-          const uint4 a = reinterpret_cast<const uint4 *>(ws)[u * (LW / 4) + q];
-          w[4 * q] = a.x; w[4 * q + 1] = a.y; w[4 * q + 2] = a.z; w[4 * q + 3] = a.w;
-        }
-      } else if constexpr (LW % 2 == 0) {
-#pragma unroll
-        for (int q = 0; q < LW / 2; ++q) {
-          const uint2 a = reinterpret_cast<const uint2 *>(ws)[u * (LW / 2) + q];
-          w[2 * q] = a.x; w[2 * q + 1] = a.y;
-        }
-      } else {
-#pragma unroll
-        for (int q = 0; q < LW; ++q) w[q] = ws[u * LW + q];
+    for (uint32_t h = 0; h < kPerSync; ++h) {
+      if (h >= n) break;
+      uint32_t st = stage + h, ph = phase;
+      if (st >= static_cast<uint32_t>(STAGES)) {
+        st -= STAGES;
+        ph ^= 1u;
       }
+      ok = mbar_wait(&full[st], ph) && ok;
+      const uint32_t *ws = reinterpret_cast<const uint32_t *>(ring + st * TILE_BYTES);
+      float c0 = 0.f, c1 = 0.f;
 #pragma unroll
-      for (int i = 0; i < UV * GROUP; ++i) {
-        const float m = __uint_as_float(field_top<S, W>(w, i));
-        if (i & 1)
-          c1 = fmaf(m, vec[v * UV * GROUP + i], c1);
-        else
-          c0 = fmaf(m, vec[v * UV * GROUP + i], c0);
+      for (int v = 0; v < V / GROUP; ++v) {
+        const int u = threadIdx.x + v * kThreads;
+        uint32_t w[LW];
+        if constexpr (LW % 4 == 0) {
+#pragma unroll
+          for (int q = 0; q < LW / 4; ++q) {
+            const uint4 a = reinterpret_cast<const uint4 *>(ws)[u * (LW / 4) + q];
+            w[4 * q] = a.x; w[4 * q + 1] = a.y; w[4 * q + 2] = a.z; w[4 * q + 3] = a.w;
+          }
+        } else if constexpr (LW % 2 == 0) {
+#pragma unroll
+          for (int q = 0; q < LW / 2; ++q) {
+            const uint2 a = reinterpret_cast<const uint2 *>(ws)[u * (LW / 2) + q];
+            w[2 * q] = a.x; w[2 * q + 1] = a.y;
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < LW; ++q) w[q] = ws[u * LW + q];
+        }
+#pragma unroll
+        for (int i = 0; i < UV * GROUP; ++i) {
+          const uint32_t m = field_top<S, W>(w, i);
+          const int j = v * UV * GROUP + i;
+          if constexpr (kPairs) {
+            if (j & 1)
+              c1 = fma_bf16<true>(m, vec2[j >> 1], c1);
+            else
+              c0 = fma_bf16<false>(m, vec2[j >> 1], c0);
+          } else if (i & 1) {
+            c1 = fmaf(__uint_as_float(m), vec[j], c1);
+          } else {
+            c0 = fmaf(__uint_as_float(m), vec[j], c0);
+          }
+        }
       }
+      red[(k + h) * kThreads + threadIdx.x] =
+          static_cast<double>(c0) + static_cast<double>(c1);
     }
-    red[k * kThreads + threadIdx.x] = static_cast<double>(c0) + static_cast<double>(c1);
-    // every thread is done with this stage, and red[k] is complete, before
-    // the stage is refilled or the group reduced
+    // every thread is done with these stages, and their rows of red are
+    // complete, before the stages are refilled or the group reduced
     if (__syncthreads_or(ok ? 0 : 1)) {
       failed = true;
       break;
     }
-    if (threadIdx.x == 0 && t + STAGES < tiles) {
+    if (threadIdx.x == 0) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(t + STAGES, stage);
+      for (uint32_t h = 0; h < n; ++h) {
+        uint32_t st = stage + h;
+        if (st >= static_cast<uint32_t>(STAGES)) st -= STAGES;
+        if (t + h + STAGES < tiles) issue(t + h + STAGES, st);
+      }
     }
-    if (++stage == static_cast<uint32_t>(STAGES)) {
-      stage = 0;
+    stage += n;
+    if (stage >= static_cast<uint32_t>(STAGES)) {
+      stage -= STAGES;
       phase ^= 1u;
     }
-    if (++k == static_cast<uint32_t>(kGemvRows) || t + 1 == tiles) {
-      // one warp per row of the group: 8 partials per lane, then the warp
+    k += n;
+    if (k == static_cast<uint32_t>(kGemvRows) || t + n == tiles) {
+      // one warp per row of the group: lane l adds partials l, l + 32, ...
+      // (conflict-free), then the warp's fixed tree
       const uint32_t row = threadIdx.x >> 5, lane = threadIdx.x & 31;
       if (row < k) {
-        const double *p = red + row * kThreads + lane * 8;
+        const double *p = red + row * kThreads + lane;
         double s = 0.0;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) s += p[j];
+        for (int j = 0; j < kThreads / 32; ++j) s += p[32 * j];
         s = warp_sum(s);
         if (lane == 0) gemv_publish(g, first_row + done + row, s);
       }
