@@ -182,3 +182,27 @@ def test_gemv_vector_once_special_values(ws, orc):
             assert got[r] == want, (r, got[r], want)
         else:
             assert np.isfinite(got[r]), r
+
+
+@pytest.mark.parametrize("name", ["e8m0", "e8m5", "e8m15"])
+def test_gemv_whole_segments_on_the_batch_path(ws, orc, name):
+    """Whole-segment shapes that the vector-once kernel does not take: the
+    FP64 accumulator, the LDG strategy, and a matrix that does not start on
+    a 16-byte boundary (value-index rows on the per-value path)."""
+    import torch
+    from accessor_universal_test_b200 import _lib
+    rows, columns = 19, 16384
+    m, v, ref = _operands(ws, orc, name, 0, rows, columns)
+    got = _gemv(ws, name, 0, 1, m, v, rows, columns)
+    _check_rows(got, ref, 1, rows, (name, "fp64"))
+    got = _gemv(ws, name, 0, 0, m, v, rows, columns, strategy=1)
+    _check_rows(got, ref, 0, rows, (name, "ldg"))
+    # the same matrix copied 4 bytes into a larger buffer
+    shifted = torch.zeros(m.numel() + 16, dtype=torch.uint8, device="cuda")
+    shifted[4:4 + m.numel()] = m
+    out = torch.full((rows,), float("nan"), dtype=torch.float64, device="cuda")
+    ws.gemv(_lib.format_id(name), 0, 0, shifted.data_ptr() + 4, v.data_ptr(), rows, columns,
+            out.data_ptr())
+    torch.cuda.synchronize()
+    assert ws.status() == 0
+    _check_rows(out.cpu().numpy(), ref, 0, rows, (name, "unaligned"))
