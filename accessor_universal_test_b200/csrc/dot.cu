@@ -1062,27 +1062,14 @@ constexpr int tma_ring(int s, bool fp64) {
 // run a second instantiation with the 64 KiB ring (`Short`). The ring depth
 // stays a compile-time constant: read from the launch parameters instead,
 // it cost the 10-bit codes 14 % (6337 -> 5475 GB/s).
-// A codec may set its own ring (kTmaRing, bytes) and codes per thread per
-// tile (kTmaVpt); 0 keeps the defaults above.
-template <class Codec, class = void> struct tma_overrides {
-  static constexpr int ring = 0, vpt = 0;
-};
-template <class Codec>
-struct tma_overrides<Codec, std::void_t<decltype(Codec::kTmaRing), decltype(Codec::kTmaVpt)>> {
-  static constexpr int ring = Codec::kTmaRing, vpt = Codec::kTmaVpt;
-};
-
 template <class Codec, class Acc, bool Short>
 constexpr int tma_ring_of() {
-  if (tma_overrides<Codec>::ring != 0) return tma_overrides<Codec>::ring;
   if (Codec::kTableBytes > 1024) return 32 * 1024;
   return Short ? 64 * 1024 : tma_ring(Codec::kS, std::is_same_v<Acc, acc_f64>);
 }
 
 template <class Codec, class Acc, bool Short = false>
-using tma_shape_of =
-    tma_shape<Codec::kS, tma_ring_of<Codec, Acc, Short>(),
-              (tma_overrides<Codec>::vpt != 0 ? tma_overrides<Codec>::vpt : tma_vpt(Codec::kS))>;
+using tma_shape_of = tma_shape<Codec::kS, tma_ring_of<Codec, Acc, Short>()>;
 
 // Whether the codec's single-DOT ring is deeper than the batched one.
 template <class Codec, class Acc>
