@@ -143,7 +143,10 @@ double aut_packed_bytes(int32_t format, uint64_t n);
 typedef struct aut_workspace aut_workspace;
 /* Allocates the grid-reduction scratch and binds the library to `device`.
  * Replaces the reference's partials/result buffers
- * (src/bitwidth_strategy_bench.cu:466, device_buffer<value_type> partials_(512)). */
+ * (src/bitwidth_strategy_bench.cu:466, device_buffer<value_type> partials_(512)).
+ * Every DOT and GEMV call on a workspace uses its one scratch area: calls on
+ * one stream follow each other; streams that run calls at the same time need
+ * a workspace each. */
 aut_status aut_workspace_create(int32_t device, aut_workspace **out);
 aut_status aut_workspace_destroy(aut_workspace *ws);
 /* Builds (once) the decode tables of `format` so that later calls issue no
