@@ -1274,12 +1274,16 @@ struct gemv_params {
   const unsigned char *vector;
   uint64_t row_bytes;
   uint32_t rows;               // rows of this launch
-  uint32_t groups_per_block;   // groups of kGemvRows rows
+  uint32_t groups_per_block;   // groups of gemv_rows<Codec>() rows
   double *partials;            // [rows][gridDim.x]
   unsigned int *status;
 };
 
-constexpr int kGemvRows = kThreads / 32;  // rows per group: one warp per row
+// Rows per group (at most one warp per row): 4 for 9-bit codes, whose
+// 18 KiB tiles leave room for a third ring stage when the row staging
+// halves (e8m0 4590 -> 4859 GB/s), 8 for the others (e8m5 5685 at 8 rows,
+// 5443 at 4).
+template <class Codec> constexpr int gemv_rows() { return Codec::kS == 9 ? 4 : kThreads / 32; }
 
 // c + a * b for two bf16 values, exact product, one rounding (the sm_100
 // mixed-precision FMA): `a_top` holds a in its high half (FP32 bits whose low
@@ -1307,8 +1311,9 @@ __device__ __forceinline__ float fma_bf16(uint32_t a_top, uint32_t pair, float c
 // figure).  From sweeps of 64-256 on B200 (1024 x 2^17, FP32, GB/s at 96 /
 // 128): e8m0 4590 / 4322, e8m1 5107 / 4480, e8m3 5408 / 5224, e8m5 5651 /
 // 5477, bf16 5829 / 5934, e8m15 6284 / 6282: beside the 16 KiB row staging a
-// bigger ring costs a block per SM, except for 16-bit codes.
-constexpr int gemv_ring(int s) { return (s == 16 ? 128 : 96) * 1024; }
+// bigger ring costs a block per SM, except for 16-bit codes; 9-bit codes
+// stage 8 KiB of rows and take the third stage (see gemv_rows).
+constexpr int gemv_ring(int s) { return (s == 16 || s == 9 ? 128 : 96) * 1024; }
 
 template <class Codec>
 using gemv_shape = tma_shape<Codec::kS, gemv_ring(Codec::kS),
@@ -1353,10 +1358,11 @@ __global__ void __launch_bounds__(kThreads, Codec::kS == 12 ? 3 : 1)
   static_assert(VPT <= 64, "two chains of at most 32 products per row tile");
   __shared__ __align__(8) uint64_t full[STAGES];
   unsigned char *ring = smem;
-  double *red = reinterpret_cast<double *>(smem + STAGES * TILE_BYTES);  // [kGemvRows][kThreads]
+  constexpr int kRows = gemv_rows<Codec>();
+  double *red = reinterpret_cast<double *>(smem + STAGES * TILE_BYTES);  // [kRows][kThreads]
 
-  const uint32_t first_row = blockIdx.y * g.groups_per_block * kGemvRows;
-  const uint32_t end_row = min(g.rows, first_row + g.groups_per_block * kGemvRows);
+  const uint32_t first_row = blockIdx.y * g.groups_per_block * kRows;
+  const uint32_t end_row = min(g.rows, first_row + g.groups_per_block * kRows);
   const uint32_t tiles = end_row > first_row ? end_row - first_row : 0;
   const unsigned char *seg = g.matrix + static_cast<uint64_t>(blockIdx.x) * TILE_BYTES;
 
@@ -1482,7 +1488,7 @@ __global__ void __launch_bounds__(kThreads, Codec::kS == 12 ? 3 : 1)
       phase ^= 1u;
     }
     k += n;
-    if (k == static_cast<uint32_t>(kGemvRows) || t + n == tiles) {
+    if (k == static_cast<uint32_t>(kRows) || t + n == tiles) {
       // one warp per row of the group: lane l adds partials l, l + 32, ...
       // (conflict-free), then the warp's fixed tree
       const uint32_t row = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1965,6 +1971,7 @@ struct gemv_entry {
   int smem = 0;
   uint64_t tile_values = 0;
   uint64_t tile_bytes = 0;
+  int group_rows = 0;
 };
 
 template <class Codec>
@@ -1972,7 +1979,8 @@ gemv_entry make_gemv_entry() {
   using shape = aut::dev::gemv_shape<Codec>;
   gemv_entry e;
   e.fn = aut::dev::gemv_tma_kernel<Codec>;
-  e.smem = shape::STAGES * shape::TILE_BYTES + aut::dev::kGemvRows * aut::dev::kThreads * 8;
+  e.smem = shape::STAGES * shape::TILE_BYTES + aut::dev::gemv_rows<Codec>() * aut::dev::kThreads * 8;
+  e.group_rows = aut::dev::gemv_rows<Codec>();
   e.tile_values = shape::TILE_VALUES;
   e.tile_bytes = shape::TILE_BYTES;
   return e;
@@ -2043,7 +2051,7 @@ aut_status gemv_launch(aut_workspace *ws, int32_t format, int32_t layout, int32_
   if (st != AUT_OK) return st;
   const uint64_t row_bytes = segments * e.tile_bytes;
   const uint64_t cap = static_cast<uint64_t>(ws->sm_count) * per_sm;
-  const uint64_t group_rows = aut::dev::kGemvRows;
+  const uint64_t group_rows = static_cast<uint64_t>(e.group_rows);
   for (uint64_t r0 = 0; r0 < rows; r0 += kMaxBatchPerLaunch) {
     const uint64_t rc = rows - r0 < static_cast<uint64_t>(kMaxBatchPerLaunch)
                             ? rows - r0
