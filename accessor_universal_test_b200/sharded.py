@@ -53,6 +53,19 @@ def allreduce_partials(partials, group=None):
     return partials
 
 
+def allreduce_partials_async(partials, group=None):
+    """Start the in-place sum of the per-rank partials and return its work
+    handle (None on one rank).  With NCCL the collective runs on the
+    library's own stream after the kernels that wrote `partials`, so work
+    launched next on the caller's stream overlaps it; ``handle.wait()`` makes
+    the caller's stream (not the host) wait for the sum, which must happen
+    before `partials` is read or written again."""
+    import torch.distributed as dist
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
+        return dist.all_reduce(partials, op=dist.ReduceOp.SUM, group=group, async_op=True)
+    return None
+
+
 class ShardedDot:
     """Runs one DOT per rank over its shard and all-reduces the partials.
 

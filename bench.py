@@ -308,7 +308,7 @@ def main():
     import torch
     import torch.distributed as dist
     from accessor_universal_test_b200 import _lib, vectors
-    from accessor_universal_test_b200.sharded import allreduce_partials
+    from accessor_universal_test_b200.sharded import allreduce_partials, allreduce_partials_async
 
     torch.cuda.set_device(local)
     if world > 1:
@@ -339,27 +339,51 @@ def main():
         inputs.append((x, y))
         values = (rows * cols + cols) if gemv else 2 * n
         packed_bytes.append(values * _lib.format_info(fid)[1] / 8)
-    results = torch.zeros(len(fmts) * rows, dtype=torch.float64, device="cuda")
+    # two result buffers: a timed step's all-reduce overlaps the next step
+    results2 = torch.zeros(2, len(fmts) * rows, dtype=torch.float64, device="cuda")
+    results = results2[0]
     res_ptr = results.data_ptr()
     torch.cuda.synchronize()
 
-    def launch(k, strat, dec=0):
+    def launch(k, strat, dec=0, out=None):
         x, y = inputs[k]
+        base = res_ptr if out is None else out
         if gemv:
             ws.gemv(fids[k], layout, accum, x.data_ptr(), y.data_ptr(), rows, cols,
-                    res_ptr + 8 * rows * k, stream, strat, dec)
+                    base + 8 * rows * k, stream, strat, dec)
         else:
-            ws.dot(fids[k], layout, accum, x.data_ptr(), y.data_ptr(), n, res_ptr + 8 * k,
+            ws.dot(fids[k], layout, accum, x.data_ptr(), y.data_ptr(), n, base + 8 * k,
                    stream, strat, dec)
 
+    # On N > 1 GPUs each step's all-reduce of its partials runs on NCCL's
+    # stream while the next step's DOTs run; a step reusing a result buffer
+    # first makes the stream wait for the all-reduce that last used it, and
+    # drain() makes it wait for all of them, so every timed step is complete
+    # (kernels and collective) before the stop event.
+    pending = [None, None]
+    steps_run = [0]
+
     def step():
+        b = steps_run[0] & 1
+        steps_run[0] += 1
+        if pending[b] is not None:
+            pending[b].wait()
+            pending[b] = None
+        out = results2[b]
         for k in range(len(fids)):
-            launch(k, strategy)
+            launch(k, strategy, out=out.data_ptr())
         if world > 1 and not gemv:
-            allreduce_partials(results)
+            pending[b] = allreduce_partials_async(out)
+
+    def drain():
+        for b in (0, 1):
+            if pending[b] is not None:
+                pending[b].wait()
+                pending[b] = None
 
     for _ in range(args.warmup):
         step()
+    drain()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -370,6 +394,7 @@ def main():
         start.record()
         for _ in range(args.steps):
             step()
+        drain()
         stop.record()
         torch.cuda.synchronize()
     ms = start.elapsed_time(stop)

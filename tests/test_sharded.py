@@ -108,3 +108,40 @@ def test_a_failing_rank_surfaces_as_an_error_not_a_hang():
     res = _run(2, "e8m0", 10_000, fail_rank=1)
     assert res[1][1] == "error"          # the failing rank reports its exception
     assert res[0][1] == "error"          # the survivor's collective fails by timeout
+
+
+def _async_worker(rank, world, port, q):
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path.insert(0, os.path.dirname(here))
+    from accessor_universal_test_b200.sharded import allreduce_partials_async
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=10))
+    try:
+        # two buffers in flight at once, as the benchmark's overlapped steps use them
+        a = torch.tensor([1.0 + rank, 10.0 * rank], dtype=torch.float64)
+        b = torch.tensor([0.5 * rank, -3.0], dtype=torch.float64)
+        wa = allreduce_partials_async(a)
+        wb = allreduce_partials_async(b)
+        wa.wait()
+        wb.wait()
+        q.put((rank, a.tolist(), b.tolist()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_async_allreduce_of_two_buffers_in_flight():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_async_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = sorted(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    for _, a, b in out:
+        assert a == [3.0, 10.0] and b == [0.5, -6.0]
+    from accessor_universal_test_b200.sharded import allreduce_partials_async
+    assert allreduce_partials_async(torch.zeros(1)) is None  # one rank: nothing to do
