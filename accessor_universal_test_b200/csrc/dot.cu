@@ -1050,7 +1050,8 @@ struct tma_shape {
 // 6514 (160), 24 bits 6829 -> 6895 (128); 6 bits keeps 64 KiB (5429; 4266 at
 // 128).  The winners hold one block per SM with four to six stages in flight.
 // The FP64 accumulator keeps 64 KiB: its longer per-pair work wants more
-// warps instead (e8m0 5751 at 64 KiB, 4748 at 160).
+// warps instead (e8m0 5751 at 64 KiB, 4748 at 160; halving e8m0's tile to 32
+// codes per thread: 5457 at 64 KiB, 5104 at 96).
 constexpr int tma_ring(int s, bool fp64) {
   if (fp64) return 64 * 1024;
   return s == 9 || s == 14 ? 160 * 1024 : (s == 10 || s == 12 || s == 24 ? 128 * 1024 : 64 * 1024);
