@@ -179,6 +179,7 @@ struct f64_codec {
 template <int S> struct e2m3_codec {
   static_assert(S == 6 || S == 8, "dense 6-bit or one code per byte");
   static constexpr int kS = S;
+  static constexpr int kW = 6;
   static constexpr int kU = S == 8 ? 4 : 2;
   // dense: two multipliers in shared memory (see bytes4)
   static constexpr int kTableBytes = S == 6 ? 16 : 0;
@@ -1256,8 +1257,8 @@ __global__ void __launch_bounds__(kThreads)
 
 
 // ---------------------------------------------------------------------------
-// GEMV with the vector decoded once per block (FP32 accumulation, E8 codes
-// and raw FP32).  Block (s, b) owns column segment s -- one tile of the DOT
+// GEMV with the vector decoded once per block (FP32 accumulation of the E8
+// codes and raw FP32; e2m3, exact, with either accumulator).  Block (s, b) owns column segment s -- one tile of the DOT
 // kernels' shape, so one bulk copy per row -- and the contiguous rows of
 // groups [b * groups_per_block, (b + 1) * groups_per_block).  It decodes its
 // vector segment into registers once, streams its rows' tiles through the
@@ -1280,11 +1281,17 @@ struct gemv_params {
   unsigned int *status;
 };
 
+template <class Codec> struct is_e2m3 : std::false_type {};
+template <int S> struct is_e2m3<e2m3_codec<S>> : std::true_type {};
+
 // Rows per group (at most one warp per row): 4 for 9-bit codes, whose
 // 18 KiB tiles leave room for a third ring stage when the row staging
-// halves (e8m0 4590 -> 4859 GB/s), 8 for the others (e8m5 5685 at 8 rows,
-// 5443 at 4).
-template <class Codec> constexpr int gemv_rows() { return Codec::kS == 9 ? 4 : kThreads / 32; }
+// halves (e8m0 4590 -> 4859 GB/s), and for dense e2m3, which fits another
+// block per SM (3038 -> 3348); 8 for the others (e8m5 5685 at 8 rows, 5443
+// at 4).
+template <class Codec> constexpr int gemv_rows() {
+  return Codec::kS == 9 || Codec::kS == 6 ? 4 : kThreads / 32;
+}
 
 // c + a * b for two bf16 values, exact product, one rounding (the sm_100
 // mixed-precision FMA): `a_top` holds a in its high half (FP32 bits whose low
@@ -1358,9 +1365,10 @@ __global__ void __launch_bounds__(kThreads, Codec::kS == 12 ? 3 : 1)
   constexpr int TILE_BYTES = shape::TILE_BYTES;
   static_assert(VPT <= 64, "two chains of at most 32 products per row tile");
   __shared__ __align__(8) uint64_t full[STAGES];
-  unsigned char *ring = smem;
+  unsigned char *ring = smem + Codec::kTableBytes;
   constexpr int kRows = gemv_rows<Codec>();
-  double *red = reinterpret_cast<double *>(smem + STAGES * TILE_BYTES);  // [kRows][kThreads]
+  double *red = reinterpret_cast<double *>(ring + STAGES * TILE_BYTES);  // [kRows][kThreads]
+  constexpr bool kE2m3 = is_e2m3<Codec>::value;
 
   const uint32_t first_row = blockIdx.y * g.groups_per_block * kRows;
   const uint32_t end_row = min(g.rows, first_row + g.groups_per_block * kRows);
@@ -1377,13 +1385,15 @@ __global__ void __launch_bounds__(kThreads, Codec::kS == 12 ? 3 : 1)
     for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1);
     mbar_fence_init();
   }
+  if constexpr (Codec::kTableBytes > 0) Codec::prepare(dot_params{}, smem);
   __syncthreads();
   if (threadIdx.x == 0)
     for (uint32_t t = 0; t < tiles && t < static_cast<uint32_t>(STAGES); ++t) issue(t, t);
 
   // this thread's codes of the vector segment, decoded once: codes of up to
   // 16 bits are bf16 values exactly and are kept as bf16 pairs (half the
-  // registers, so more blocks fit an SM); wider ones as FP32
+  // registers, so more blocks fit an SM); wider ones as FP32; e2m3 codes as
+  // the f16 pairs of the hardware conversion
   constexpr bool kPairs = W <= 16;
   float vec[kPairs ? 1 : VPT];
   uint32_t vec2[kPairs ? VPT / 2 : 1];
@@ -1396,6 +1406,14 @@ __global__ void __launch_bounds__(kThreads, Codec::kS == 12 ? 3 : 1)
       uint32_t w[LW];
 #pragma unroll
       for (int q = 0; q < LW; ++q) w[q] = __ldg(vw + u * LW + q);
+      if constexpr (kE2m3) {
+#pragma unroll
+        for (int q = 0; q < UV * GROUP / 4; ++q) {
+          const int j = (v * UV * GROUP) / 2 + 2 * q;  // f16 pair index
+          Codec::to_f16x2x2(Codec::bytes4(w, q, smem), vec2[j], vec2[j + 1]);
+        }
+        continue;
+      }
 #pragma unroll
       for (int i = 0; i < UV * GROUP; ++i) {
         const uint32_t bits = field_top<S, W>(w, i);
@@ -1449,6 +1467,19 @@ __global__ void __launch_bounds__(kThreads, Codec::kS == 12 ? 3 : 1)
         } else {
 #pragma unroll
           for (int q = 0; q < LW; ++q) w[q] = ws[u * LW + q];
+        }
+        if constexpr (kE2m3) {
+          // products of two f16 values into FP32, exactly (e2m3_codec::fma2):
+          // c0 takes the even codes, c1 the odd ones
+#pragma unroll
+          for (int q = 0; q < UV * GROUP / 4; ++q) {
+            const int j = (v * UV * GROUP) / 2 + 2 * q;
+            uint32_t lo, hi;
+            Codec::to_f16x2x2(Codec::bytes4(w, q, smem), lo, hi);
+            Codec::fma2(c0, c1, lo, vec2[j]);
+            Codec::fma2(c0, c1, hi, vec2[j + 1]);
+          }
+          continue;
         }
 #pragma unroll
         for (int i = 0; i < UV * GROUP; ++i) {
@@ -1980,7 +2011,8 @@ gemv_entry make_gemv_entry() {
   using shape = aut::dev::gemv_shape<Codec>;
   gemv_entry e;
   e.fn = aut::dev::gemv_tma_kernel<Codec>;
-  e.smem = shape::STAGES * shape::TILE_BYTES + aut::dev::gemv_rows<Codec>() * aut::dev::kThreads * 8;
+  e.smem = Codec::kTableBytes + shape::STAGES * shape::TILE_BYTES +
+           aut::dev::gemv_rows<Codec>() * aut::dev::kThreads * 8;
   e.group_rows = aut::dev::gemv_rows<Codec>();
   e.tile_values = shape::TILE_VALUES;
   e.tile_bytes = shape::TILE_BYTES;
@@ -1998,6 +2030,7 @@ static gemv_entry gemv_lookup(int32_t format, int32_t layout) {
   case AUT_FMT_E8M5: return dense ? make_gemv_entry<e8_codec<14, 14>>() : make_gemv_entry<e8_codec<16, 14>>();
   case AUT_FMT_BF16_E8M7: return make_gemv_entry<e8_codec<16, 16>>();
   case AUT_FMT_E8M15: return dense ? make_gemv_entry<e8_codec<24, 24>>() : make_gemv_entry<e8_codec<32, 24>>();
+  case AUT_FMT_E2M3: return dense ? make_gemv_entry<e2m3_codec<6>>() : make_gemv_entry<e2m3_codec<8>>();
   default: return {};
   }
 }
@@ -2028,8 +2061,9 @@ static aut_status gemv_blocks_per_sm(const gemv_entry &e, int *out) {
   return AUT_OK;
 }
 
-// The GEMV path that decodes the vector once per block: FP32 accumulation,
-// the E8 codes and raw FP32, decoder AUTO/DIRECT, strategy AUTO/TMA, whole
+// The GEMV path that decodes the vector once per block: FP32 accumulation
+// of the E8 codes and raw FP32, either accumulator for e2m3 (exact), decoder
+// AUTO/DIRECT, strategy AUTO/TMA, whole
 // segments (columns a multiple of one tile) and 16-byte aligned operands.
 // *handled is false when the call does not qualify; aut_gemv then runs the
 // rows as a batch of DOTs.
@@ -2038,7 +2072,8 @@ aut_status gemv_launch(aut_workspace *ws, int32_t format, int32_t layout, int32_
                        const void *vector, uint64_t rows, uint64_t columns,
                        double *results, void *stream, bool *handled) {
   *handled = false;
-  if (accum != AUT_ACCUM_FP32) return AUT_OK;
+  // e2m3 rows are exact up to their final rounding with either accumulator
+  if (accum != AUT_ACCUM_FP32 && format != AUT_FMT_E2M3) return AUT_OK;
   if (strategy != AUT_STRATEGY_AUTO && strategy != AUT_STRATEGY_TMA) return AUT_OK;
   if (decoder != AUT_DECODER_AUTO && decoder != AUT_DECODER_DIRECT) return AUT_OK;
   const gemv_entry e = gemv_lookup(format, layout);

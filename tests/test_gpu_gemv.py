@@ -125,7 +125,7 @@ def test_gemv_degenerate_shapes(ws):
 # The FP32 GEMV of the E8 codes and raw FP32 decodes the vector once per block
 # when the columns are whole segments (one bulk-copy tile per row: 16384
 # values for 9-bit codes, 8192 for the others).
-VECTOR_ONCE = ["e8m0", "e8m1", "e8m3", "e8m5", "bf16_e8m7", "e8m15", "fp32"]
+VECTOR_ONCE = ["e8m0", "e8m1", "e8m3", "e8m5", "bf16_e8m7", "e8m15", "fp32", "e2m3"]
 
 
 @pytest.mark.parametrize("name", VECTOR_ONCE)
@@ -206,3 +206,17 @@ def test_gemv_whole_segments_on_the_batch_path(ws, orc, name):
     torch.cuda.synchronize()
     assert ws.status() == 0
     _check_rows(out.cpu().numpy(), ref, 0, rows, (name, "unaligned"))
+
+
+@pytest.mark.parametrize("layout", [0, 1])
+@pytest.mark.parametrize("accum", [0, 1])
+def test_gemv_e2m3_rows_are_exact(ws, orc, layout, accum):
+    """e2m3 products and their partial sums are exact, so every row of the
+    vector-once GEMV is the exact row sum rounded once, with either
+    accumulator."""
+    rows, columns = 21, 32768
+    m, v, ref = _operands(ws, orc, "e2m3", layout, rows, columns)
+    got = _gemv(ws, "e2m3", layout, accum, m, v, rows, columns)
+    for r in range(rows):
+        d, _ = ref(r)
+        assert got[r] == float(np.longdouble(d[0]) + np.longdouble(d[1])), (layout, accum, r)
