@@ -18,6 +18,8 @@ AUT_ERR_UNSUPPORTED = 2
 AUT_ERR_CUDA = 3
 AUT_ERR_TOO_LARGE = 4
 AUT_ERR_NO_DEVICE = 5
+AUT_ERR_COMM = 6
+COMM_ID_BYTES = 128
 
 FAMILY_BINARY, FAMILY_PREFIX, FAMILY_LNS, FAMILY_RAW_FP32, FAMILY_RAW_FP64 = range(5)
 DENSE, PADDED = 0, 1
@@ -25,7 +27,7 @@ ACC_FP32, ACC_FP64 = 0, 1
 TARGET_FP32, TARGET_FP64 = 0, 1
 STRATEGY_AUTO, STRATEGY_LDG, STRATEGY_TMA, STRATEGY_SCALAR = 0, 1, 2, 3
 (DECODER_AUTO, DECODER_DIRECT, DECODER_FULL_LUT, DECODER_FRACTION_LUT,
- DECODER_FRACTION_LUT_FUSED, DECODER_FUSED_SUM_LUT) = range(6)
+ DECODER_FRACTION_LUT_FUSED, DECODER_FUSED_SUM_LUT, DECODER_EX2_APPROX) = range(7)
 STATUS_WAIT_TIMEOUT = 1
 GEN_SIGNED_UNIT_F64, GEN_SIGNED_UNIT_F32, GEN_NORMAL, GEN_LNS_CANCEL, GEN_POSITIVE_UNIT_F64 = range(5)
 
@@ -49,12 +51,19 @@ SIGNATURES = {
     "aut_workspace_prepare": (_i32, [_vp, _i32]),
     "aut_workspace_info": (_i32, [_vp, _i32p, _i32p]),
     "aut_workspace_status": (_i32, [_vp, C.POINTER(_u32), _i32]),
+    "aut_workspace_inject_stall": (_i32, [_vp, _u64, _u64]),
     "aut_dot": (_i32, [_vp, _i32, _i32, _i32, _vp, _vp, _u64, _vp, _vp]),
     "aut_dot_strategy": (_i32, [_vp, _i32, _i32, _i32, _i32, _vp, _vp, _u64, _vp, _vp]),
     "aut_dot_variant": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _u64, _vp, _vp]),
     "aut_dot_batched": (_i32, [_vp, _i32, _i32, _i32, _vp, _vp, _u64, _u32, _u64, _vp, _vp]),
     "aut_gemv": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _u64, _u64, _vp, _vp]),
     "aut_dot_noalloc": (_i32, [_i32, _i32, _i32, _vp, _vp, _u64, _u32, _u64, _vp, _vp]),
+    "aut_comm_unique_id": (_i32, [_vp]),
+    "aut_comm_create": (_i32, [_vp, _i32, _i32, _i32, C.POINTER(_vp)]),
+    "aut_comm_wrap": (_i32, [_vp, _i32, C.POINTER(_vp)]),
+    "aut_comm_destroy": (_i32, [_vp]),
+    "aut_comm_allreduce": (_i32, [_vp, _vp, _u64, _vp]),
+    "aut_dot_sharded": (_i32, [_vp, _vp, _i32, _i32, _i32, _vp, _vp, _u64, _vp, _vp]),
     "aut_decode": (_i32, [_vp, _i32, _i32, _i32, _vp, _u64, _vp, _vp]),
     "aut_encode": (_i32, [_vp, _i32, _i32, _vp, _u64, _vp, _vp]),
     "aut_generate": (_i32, [_i32, _u64, _i32, _u64, _u64, _vp, _vp]),
@@ -150,6 +159,11 @@ class Workspace:
         check(load().aut_workspace_status(self.handle, C.byref(word), 1 if clear else 0))
         return word.value
 
+    def inject_stall(self, stall_tile: int = 2**64 - 1, wait_cycles: int = 0) -> None:
+        """Failure-detection test hook: the bulk-copy kernels withhold the
+        copies of tile `stall_tile`, so their bounded wait runs out."""
+        check(load().aut_workspace_inject_stall(self.handle, stall_tile, wait_cycles))
+
     def dot_batched(self, fmt, layout, accum, x_ptr, y_ptr, n, batch, stride_bytes,
                     results_ptr, stream=0) -> None:
         check(load().aut_dot_batched(self.handle, fmt, layout, accum, x_ptr, y_ptr, n,
@@ -165,6 +179,37 @@ class Workspace:
 
     def encode(self, fmt, layout, values_ptr, n, codes_ptr, stream=0) -> None:
         check(load().aut_encode(self.handle, fmt, layout, values_ptr, n, codes_ptr, stream))
+
+
+def comm_unique_id() -> bytes:
+    """A fresh NCCL communicator id for Comm(); one rank makes it."""
+    buf = C.create_string_buffer(COMM_ID_BYTES)
+    check(load().aut_comm_unique_id(buf))
+    return buf.raw
+
+
+class Comm:
+    """An aut_comm: this rank's NCCL communicator for aut_dot_sharded."""
+
+    def __init__(self, unique_id: bytes, nranks: int, rank: int, device: int):
+        if len(unique_id) != COMM_ID_BYTES:
+            raise ValueError(f"communicator id must be {COMM_ID_BYTES} bytes")
+        h = C.c_void_p()
+        check(load().aut_comm_create(unique_id, nranks, rank, device, C.byref(h)))
+        self.handle = h
+
+    def close(self) -> None:
+        if self.handle:
+            check(load().aut_comm_destroy(self.handle))
+            self.handle = None
+
+    def allreduce(self, values_ptr, count: int, stream=0) -> None:
+        check(load().aut_comm_allreduce(self.handle, values_ptr, count, stream))
+
+    def dot(self, ws: "Workspace", fmt, layout, accum, x_ptr, y_ptr, n_local, result_ptr,
+            stream=0) -> None:
+        check(load().aut_dot_sharded(self.handle, ws.handle, fmt, layout, accum, x_ptr, y_ptr,
+                                     n_local, result_ptr, stream))
 
 
 def generate(kind: int, seed: int, vector_id: int, first: int, n: int, out_ptr, stream=0) -> None:

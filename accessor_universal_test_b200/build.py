@@ -73,7 +73,7 @@ def build_library(verbose: bool = False) -> str:
     with cf.ThreadPoolExecutor(max_workers=min(8, len(sources))) as ex:
         objs = list(ex.map(lambda s: _compile(s, verbose), sources))
     if _stale(LIB, objs):
-        cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcudart"]
+        cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcudart", "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -249,7 +249,7 @@ struct generic_dot_params {
 template <class Acc, bool kF32>
 __global__ void __launch_bounds__(kThreads) dot_generic_kernel(const generic_dot_params g) {
   extern __shared__ __align__(16) unsigned char table[];
-  __shared__ double scratch[kThreads / 32];
+  __shared__ double scratch[kScratchDoubles];
   codec_params c = g.codec;
   if (g.table_smem_bytes > 0) {
     const uint4 *src = kF32 ? reinterpret_cast<const uint4 *>(c.lns_f32)
@@ -295,9 +295,9 @@ __global__ void __launch_bounds__(kThreads) dot_generic_kernel(const generic_dot
     }
   }
   for (; i < g.n; i += step) mac(0, load_any(xb, c.stride, xo + i), load_any(yb, c.stride, yo + i));
-  const double s = block_sum(acc.value(), scratch);
-  grid_finish(s, g.partials + static_cast<uint64_t>(batch) * gridDim.x, g.tickets + batch,
-              g.results + batch, scratch);
+  const dd s = block_sum_dd(acc.pair(), scratch);
+  grid_finish_dd(s, g.partials + 2 * static_cast<uint64_t>(batch) * gridDim.x, g.tickets + batch,
+                 g.results + batch, scratch);
 }
 
 } // namespace aut::dev

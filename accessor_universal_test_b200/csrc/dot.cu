@@ -55,6 +55,10 @@ struct dot_params {
   double *results;        // [gridDim.y]
   unsigned int *status;   // sticky error bits (AUT_STATUS_*)
   rt_params rt;           // rt_codec only
+  long long wait_cycles;  // bound of every bulk-copy wait (SM clock cycles)
+  uint64_t stall_tile;    // failure-detection test: this tile's stage is
+                          // armed but its copies are never issued, so the
+                          // wait for it runs out (~0: none)
 };
 
 // ---------------------------------------------------------------------------
@@ -281,20 +285,41 @@ template <int S> struct e2m3_codec {
   }
 };
 
-// lns8_r3 (one code per byte): a full 256-entry decode table, replicated
-// once per lane in shared memory (entry e of lane l at element e*32 + l), so
-// that a warp's 32 lookups hit 32 different banks.  Table values come from
-// the host exp2f / exp2 and are the reference's decoded values bit for bit.
+// Copies of a small decode table in shared memory, one per lane group, so a
+// warp's lookups never share a bank: entry e of copy c at element
+// e * kCopies + c.  A warp's 4-byte loads are served together, so 4-byte
+// entries need a copy per lane; 8-byte loads are served a half warp at a
+// time (16 lanes x 8 bytes span the 32 banks once), so 16 copies of 8-byte
+// entries are conflict-free and take half the space (256 FP64 entries: 32
+// KiB instead of 64, which lets twice as many blocks share an SM).
+template <typename T> struct lane_table {
+  static constexpr int kCopies = sizeof(T) == 8 ? 16 : 32;
+  static constexpr uint32_t kEntryBytes = kCopies * static_cast<uint32_t>(sizeof(T));
+  static constexpr int bytes(int entries) { return entries * static_cast<int>(kEntryBytes); }
+  __device__ __forceinline__ static uint32_t lane_offset() {
+    return (threadIdx.x & (kCopies - 1)) * static_cast<uint32_t>(sizeof(T));
+  }
+  __device__ static void fill(T *s, const T *g, int entries) {
+    for (int e = threadIdx.x; e < entries * kCopies; e += kThreads) s[e] = g[e / kCopies];
+  }
+  // entry `code` of this lane's copy
+  __device__ __forceinline__ static T at(const unsigned char *smem, uint32_t code,
+                                         uint32_t lane_off) {
+    return *reinterpret_cast<const T *>(smem + (code * kEntryBytes + lane_off));
+  }
+};
+
+// lns8_r3 (one code per byte): a full 256-entry decode table in per-lane
+// copies (lane_table).  Table values come from the host exp2f / exp2 and are
+// the reference's decoded values bit for bit.
 template <typename T> struct lns8_codec {
+  using table = lane_table<T>;
   static constexpr int kS = 8;
   static constexpr int kU = 4;
-  static constexpr int kTableBytes = 256 * 32 * static_cast<int>(sizeof(T));
+  static constexpr int kTableBytes = table::bytes(256);
   static constexpr bool kExactLanes = false;
   __device__ static void prepare(const dot_params &p, unsigned char *smem) {
-    const void *table = p.table;
-    const T *g = static_cast<const T *>(table);
-    T *s = reinterpret_cast<T *>(smem);
-    for (int e = threadIdx.x; e < 256 * 32; e += kThreads) s[e] = g[e >> 5];
+    table::fill(reinterpret_cast<T *>(smem), static_cast<const T *>(p.table), 256);
   }
 
   // Byte k of a word is moved to bits [0, 8) by one byte permute (ALU pipe)
@@ -305,16 +330,15 @@ template <typename T> struct lns8_codec {
                                                 const uint32_t *yw, Acc &acc,
                                                 float *,
                                                 const unsigned char *smem) {
-    constexpr uint32_t kEntryBytes = 32 * sizeof(T);
-    const uint32_t lane_off = (threadIdx.x & 31) * static_cast<uint32_t>(sizeof(T));
+    const uint32_t lane_off = table::lane_offset();
 #pragma unroll
     for (int w = 0; w < NV / 4; ++w) {
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const uint32_t bx = __byte_perm(xw[w], 0u, 0x4440u + k);
         const uint32_t by = __byte_perm(yw[w], 0u, 0x4440u + k);
-        const T a = *reinterpret_cast<const T *>(smem + (bx * kEntryBytes + lane_off));
-        const T b = *reinterpret_cast<const T *>(smem + (by * kEntryBytes + lane_off));
+        const T a = table::at(smem, bx, lane_off);
+        const T b = table::at(smem, by, lane_off);
         if constexpr (sizeof(T) == 4)
           acc.mac(4 * w + k, a, b);
         else
@@ -328,9 +352,9 @@ template <typename T> struct lns8_codec {
                                                 const unsigned char *yb, uint64_t j,
                                                 Acc &acc,
                                                 const unsigned char *smem) {
-    const T *tab = reinterpret_cast<const T *>(smem) + (threadIdx.x & 31);
-    acc.mac_d(0, static_cast<double>(tab[load_code<8, 8>(xb, i) << 5]),
-              static_cast<double>(tab[load_code<8, 8>(yb, j) << 5]));
+    const uint32_t lane_off = table::lane_offset();
+    acc.mac_d(0, static_cast<double>(table::at(smem, load_code<8, 8>(xb, i), lane_off)),
+              static_cast<double>(table::at(smem, load_code<8, 8>(yb, j), lane_off)));
   }
 };
 
@@ -349,16 +373,15 @@ template <typename T> struct lns8_codec {
 // zeroes products with a zero operand, and a reserved code with its sign bit
 // set (NaN) raises a flag that makes the DOT NaN.
 template <typename T> struct lns8_fused_codec {
+  using table = lane_table<T>;
   static constexpr int kS = 8;
   static constexpr int kU = 4;
   static constexpr int kEntry = static_cast<int>(sizeof(T));
-  static constexpr int kTableBytes = 256 * 32 * kEntry;
+  static constexpr int kTableBytes = table::bytes(256);
   static constexpr bool kExactLanes = false;
 
   __device__ static void prepare(const dot_params &p, unsigned char *smem) {
-    const T *g = static_cast<const T *>(p.table);
-    T *s = reinterpret_cast<T *>(smem);
-    for (int e = threadIdx.x; e < 256 * 32; e += kThreads) s[e] = g[e >> 5];
+    table::fill(reinterpret_cast<T *>(smem), static_cast<const T *>(p.table), 256);
   }
 
   template <int K> __device__ __forceinline__ static uint32_t spread(uint32_t v) {
@@ -370,7 +393,7 @@ template <typename T> struct lns8_fused_codec {
   // entry `index` of this lane's copy, zeroed unless `mask`, sign bit `sign`
   __device__ __forceinline__ static T product(const unsigned char *smem, uint32_t index,
                                               uint32_t lane_off, uint32_t mask, uint32_t sign) {
-    const unsigned char *at = smem + (index * (32 * kEntry) + lane_off);
+    const unsigned char *at = smem + (index * table::kEntryBytes + lane_off);
     if constexpr (sizeof(T) == 4) {
       const uint32_t t = *reinterpret_cast<const uint32_t *>(at);
       return __uint_as_float((t & mask) | sign);
@@ -394,7 +417,7 @@ template <typename T> struct lns8_fused_codec {
                                                 float *,
                                                 const unsigned char *smem) {
     static_assert(NV % 4 == 0, "four codes per word");
-    const uint32_t lane_off = (threadIdx.x & 31) * static_cast<uint32_t>(kEntry);
+    const uint32_t lane_off = table::lane_offset();
     uint32_t nan = 0;
 #pragma unroll
     for (int w = 0; w < NV / 4; ++w) {
@@ -436,7 +459,7 @@ template <typename T> struct lns8_fused_codec {
       v = __hiloint2double(0x7ff80000, 0);
     } else {
       const uint32_t mask = (bx == 0 || by == 0) ? 0u : 0xffffffffu;
-      const uint32_t lane_off = (threadIdx.x & 31) * static_cast<uint32_t>(kEntry);
+      const uint32_t lane_off = table::lane_offset();
       v = static_cast<double>(product(smem, bx + by, lane_off, mask, ((cx ^ cy) & 0x80u) << 24));
     }
     acc.mac_d(0, v, 1.0);
@@ -726,6 +749,134 @@ template <typename T> struct lns16_fused_codec {
   }
 };
 
+// lns8_r3 / lns16_r11 with the hardware exponential: the reference's
+// ex2_approx decoder (ex2.approx.f32, lns_decoder_strategies.cuh:215-224)
+// with the fused multiply (:353-367).  The two log codes of a pair are added
+// as in the fused table decoders (each biased by 2^(B-2), so one 32-bit add
+// sums every lane of a word pair without carries between lanes), the sum is
+// placed in the low bits of the FP32 pattern of 2^23 -- an exact integer
+// conversion -- and one FMA by 2^-R rebiases it into the exponent argument
+// (cx + cy) / 2^R, exactly; one ex2.approx.ftz.f32 per pair then gives the
+// product's magnitude.  Zero and NaN codes follow lns::multiply_codes
+// (lns_benchmark_core.hpp:241-254) without branches: the accumulating FMA's
+// second operand is +-1, or 0 when a code of the pair is zero, and a NaN
+// code raises a flag that makes the DOT NaN.  APPROXIMATE: every product
+// carries the instruction's relative error (at most 2^-21 on B200, checked
+// exhaustively over all log sums by the tests), so the DOT's normalised
+// error bound grows by that much; it needs no table.
+template <int B, typename T> struct lns_ex2_codec {
+  static_assert(B == 8 || B == 16, "lns8_r3 and lns16_r11");
+  static constexpr int kS = B;
+  static constexpr int kU = 4;
+  static constexpr int kTableBytes = 0;
+  static constexpr bool kExactLanes = false;
+  static constexpr int kR = B == 8 ? 3 : 11;
+  static constexpr int kLanes = 32 / B;  // codes per word
+  // field of one code, its offset-binary bias, and the bias of a pair's sum
+  static constexpr uint32_t kMag = B == 8 ? 0x7f7f7f7fu : 0x7fff7fffu;
+  static constexpr uint32_t kHalf = B == 8 ? 0x40404040u : 0x40004000u;
+  static constexpr uint32_t kLive = B == 8 ? 0x7f7f7f7fu : 0x7fff7fffu;
+  static constexpr uint32_t kTop = B == 8 ? 0x80808080u : 0x80008000u;
+  // (2^23 + sum) * 2^-R - (2^23 + 2^(B-1)) * 2^-R = (cx + cy) / 2^R
+  static constexpr float kScale = 1.0f / static_cast<float>(1 << kR);
+  static constexpr float kShift =
+      -static_cast<float>((8388608.0 + static_cast<double>(1u << (B - 1))) / (1 << kR));
+
+  __device__ static void prepare(const dot_params &, unsigned char *) {}
+
+  __device__ __forceinline__ static float ex2(float a) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
+    return r;
+  }
+
+  // every byte = copies of bit 7 of byte k of v (prmt sign replication)
+  template <int K> __device__ __forceinline__ static uint32_t spread(uint32_t v) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(v), "r"(0u), "n"(0x8888 + 0x1111 * K));
+    return r;
+  }
+
+  // lane k of the pair sums h as 2^23 + sum, in FP32
+  template <int K> __device__ __forceinline__ static float placed(uint32_t h) {
+    if constexpr (B == 8)
+      return __uint_as_float(__byte_perm(h, 0x4B000000u, 0x7440 + K));
+    else
+      return __uint_as_float(__byte_perm(h, 0x4B000000u, K == 0 ? 0x7410 : 0x7432));
+  }
+
+  // the top bit of code field k, at bit 31
+  template <int K> __device__ __forceinline__ static uint32_t top_of(uint32_t v) {
+    return (v << (32 - B * (K + 1))) & 0x80000000u;
+  }
+
+  template <int K, class Acc>
+  __device__ __forceinline__ static void pair(Acc &acc, int slot, uint32_t h, uint32_t live,
+                                              uint32_t sg) {
+    const float mag = ex2(fmaf(placed<K>(h), kScale, kShift));
+    // byte holding the field's top bit: K for bytes, 2K + 1 for halfwords
+    constexpr int kByte = B == 8 ? K : 2 * K + 1;
+    const uint32_t on = spread<kByte>(live);
+    if constexpr (sizeof(T) == 4) {
+      acc.mac(slot, mag, __uint_as_float((on & 0x3f800000u) | top_of<K>(sg)));
+    } else {
+      acc.mac_d(slot, static_cast<double>(mag),
+                __hiloint2double(static_cast<int>((on & 0x3ff00000u) | top_of<K>(sg)), 0));
+    }
+  }
+
+  template <int NV, class Acc>
+  __device__ __forceinline__ static void values(const uint32_t *xw,
+                                                const uint32_t *yw, Acc &acc,
+                                                float *, const unsigned char *) {
+    static_assert(NV % kLanes == 0, "whole words");
+    uint32_t nan = 0;
+#pragma unroll
+    for (int w = 0; w < NV / kLanes; ++w) {
+      const uint32_t x = xw[w], y = yw[w];
+      const uint32_t bx = (x & kMag) ^ kHalf, by = (y & kMag) ^ kHalf;
+      const uint32_t h = bx + by;  // lane k: cx + cy + 2^(B-1)
+      // top bit of each lane: that code is not reserved
+      const uint32_t lx = bx + kLive, ly = by + kLive;
+      nan |= (x & ~lx) | (y & ~ly);  // reserved with the sign bit set
+      const uint32_t live = lx & ly;
+      const uint32_t sg = x ^ y;
+      pair<0>(acc, kLanes * w, h, live, sg);
+      pair<1>(acc, kLanes * w + 1, h, live, sg);
+      if constexpr (B == 8) {
+        pair<2>(acc, kLanes * w + 2, h, live, sg);
+        pair<3>(acc, kLanes * w + 3, h, live, sg);
+      }
+    }
+    if (nan & kTop) {
+      if constexpr (sizeof(T) == 4)
+        acc.mac(0, __uint_as_float(0x7fc00000u), 1.0f);
+      else
+        acc.mac_d(0, __hiloint2double(0x7ff80000, 0), 1.0);
+    }
+  }
+
+  template <class Acc>
+  __device__ __forceinline__ static void scalar(const unsigned char *xb, uint64_t i,
+                                                const unsigned char *yb, uint64_t j,
+                                                Acc &acc, const unsigned char *) {
+    constexpr uint32_t field = (1u << (B - 1)) - 1u, half = 1u << (B - 2);
+    const uint32_t cx = load_code<B, B>(xb, i), cy = load_code<B, B>(yb, j);
+    const uint32_t bx = (cx & field) ^ half, by = (cy & field) ^ half;
+    double v;
+    if ((bx == 0 && (cx >> (B - 1))) || (by == 0 && (cy >> (B - 1)))) {
+      v = __hiloint2double(0x7ff80000, 0);
+    } else if (bx == 0 || by == 0) {
+      v = 0.0;
+    } else {
+      const float a = static_cast<float>(static_cast<int>(bx + by) - (1 << (B - 1))) * kScale;
+      v = static_cast<double>(ex2(a));
+      if ((cx ^ cy) >> (B - 1)) v = -v;
+    }
+    acc.mac_d(0, v, 1.0);
+  }
+};
+
 // Formats with codes of at most 8 bits and no dedicated codec (bit formats
 // and LNS alike): the full decode table of the format, built on the host
 // from the host decoder, replicated once per lane in shared memory (entry e
@@ -786,18 +937,16 @@ template <int S, int W, typename T> struct wide_lut_codec {
 
 template <int S, typename T> struct lut_codec {
   static_assert(S >= 2 && S <= 8, "codes of 2 to 8 bits");
+  using table = lane_table<T>;
   static constexpr int kS = S;
   static constexpr int kU = packet_shape<S>::Q == 1 ? 4 : 1;
   static constexpr int kEntries = 1 << S;
-  static constexpr int kTableBytes = kEntries * 32 * static_cast<int>(sizeof(T));
+  static constexpr int kTableBytes = table::bytes(kEntries);
   static constexpr bool kExactLanes = false;
-  static constexpr uint32_t kEntryBytes = 32 * sizeof(T);
 
   __device__ static void prepare(const dot_params &p, unsigned char *smem) {
-    const T *g = static_cast<const T *>(p.table);
-    T *s = reinterpret_cast<T *>(smem);
-    const int entries = 1 << p.rt.bits;  // the format's codes (<= kEntries)
-    for (int e = threadIdx.x; e < entries * 32; e += kThreads) s[e] = g[e >> 5];
+    // the format's codes (<= kEntries)
+    table::fill(reinterpret_cast<T *>(smem), static_cast<const T *>(p.table), 1 << p.rt.bits);
   }
 
   __device__ __forceinline__ static uint32_t code(const uint32_t *w, int v) {
@@ -811,11 +960,11 @@ template <int S, typename T> struct lut_codec {
   __device__ __forceinline__ static void values(const uint32_t *xw,
                                                 const uint32_t *yw, Acc &acc,
                                                 float *, const unsigned char *smem) {
-    const uint32_t lane_off = (threadIdx.x & 31) * static_cast<uint32_t>(sizeof(T));
+    const uint32_t lane_off = table::lane_offset();
 #pragma unroll
     for (int v = 0; v < NV; ++v) {
-      const T a = *reinterpret_cast<const T *>(smem + (code(xw, v) * kEntryBytes + lane_off));
-      const T b = *reinterpret_cast<const T *>(smem + (code(yw, v) * kEntryBytes + lane_off));
+      const T a = table::at(smem, code(xw, v), lane_off);
+      const T b = table::at(smem, code(yw, v), lane_off);
       if constexpr (sizeof(T) == 4)
         acc.mac(v, a, b);
       else
@@ -827,9 +976,9 @@ template <int S, typename T> struct lut_codec {
   __device__ __forceinline__ static void scalar(const unsigned char *xb, uint64_t i,
                                                 const unsigned char *yb, uint64_t j,
                                                 Acc &acc, const unsigned char *smem) {
-    const T *tab = reinterpret_cast<const T *>(smem) + (threadIdx.x & 31);
-    acc.mac_d(0, static_cast<double>(tab[load_code<S, S>(xb, i) << 5]),
-              static_cast<double>(tab[load_code<S, S>(yb, j) << 5]));
+    const uint32_t lane_off = table::lane_offset();
+    acc.mac_d(0, static_cast<double>(table::at(smem, load_code<S, S>(xb, i), lane_off)),
+              static_cast<double>(table::at(smem, load_code<S, S>(yb, j), lane_off)));
   }
 };
 
@@ -947,7 +1096,7 @@ template <class Codec, class Acc>
 __global__ void __launch_bounds__(kThreads)
     dot_ldg_kernel(const dot_params p) {
   extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ double scratch[kThreads / 32];
+  __shared__ double scratch[kScratchDoubles];
   constexpr int S = Codec::kS;
   constexpr int Q = packet_shape<S>::Q;
   constexpr int P = packet_shape<S>::P;
@@ -996,9 +1145,9 @@ __global__ void __launch_bounds__(kThreads)
   flush_tile<Codec>(acc, lanes);
 
   ragged_tail<Codec>(xb, xo, yb, yo, tiles * tile_packets * P, p.n, acc, smem);
-  const double s = block_sum(acc.value(), scratch);
-  grid_finish(s, p.partials + static_cast<uint64_t>(batch) * gridDim.x,
-              p.tickets + batch, p.results + batch, scratch);
+  const dd s = block_sum_dd(acc.pair(), scratch);
+  grid_finish_dd(s, p.partials + 2 * static_cast<uint64_t>(batch) * gridDim.x,
+                 p.tickets + batch, p.results + batch, scratch);
 }
 
 // ---------------------------------------------------------------------------
@@ -1067,7 +1216,9 @@ constexpr int tma_ring(int s, bool fp64) {
 template <class Codec, class Acc, bool Short>
 constexpr int tma_ring_of() {
   if (Codec::kTableBytes > 1024) return 32 * 1024;
-  return Short ? 64 * 1024 : tma_ring(Codec::kS, std::is_same_v<Acc, acc_f64>);
+  return Short ? 64 * 1024
+               : tma_ring(Codec::kS,
+                          !std::is_same_v<Acc, acc_f32> && !std::is_same_v<Acc, acc_f32c>);
 }
 
 template <class Codec, class Acc, bool Short = false>
@@ -1078,7 +1229,7 @@ template <class Codec, class Acc>
 constexpr bool has_short_ring =
     tma_shape_of<Codec, Acc, false>::STAGES != tma_shape_of<Codec, Acc, true>::STAGES;
 
-constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 2 GHz
+constexpr long long kWaitCycles = aut::kWaitCyclesDefault;
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -1101,7 +1252,7 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
                : "memory");
 }
 
-// Returns false when the phase did not complete within kWaitCycles.
+// Returns false when the phase did not complete within `limit` cycles.
 __device__ __forceinline__ bool mbar_try(uint32_t addr, uint32_t parity) {
   uint32_t done;
   asm volatile(
@@ -1116,13 +1267,14 @@ __device__ __forceinline__ bool mbar_try(uint32_t addr, uint32_t parity) {
 
 // The common case (the tile has landed) costs one try_wait; the clock is
 // read only once the first try fails, and then every 32 tries.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
+                                          long long limit = kWaitCycles) {
   const uint32_t addr = smem_addr(bar);
   if (mbar_try(addr, parity)) return true;
   const long long start = clock64();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try(addr, parity)) return true;
-    if ((i & 31u) == 0u && clock64() - start > kWaitCycles) return false;
+    if ((i & 31u) == 0u && clock64() - start > limit) return false;
   }
 }
 
@@ -1139,7 +1291,7 @@ template <class Codec, class Acc, bool Short = false>
 __global__ void __launch_bounds__(kThreads)
     dot_tma_kernel(const dot_params p) {
   extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ double scratch[kThreads / 32];
+  __shared__ double scratch[kScratchDoubles];
   using shape = tma_shape_of<Codec, Acc, Short>;
   constexpr int UV = shape::UV;
   constexpr int V = shape::V;
@@ -1165,6 +1317,7 @@ __global__ void __launch_bounds__(kThreads)
     unsigned char *dst = ring + stage * (2 * TILE_BYTES);
     uint64_t *bar = &full[stage];
     mbar_expect_tx(bar, 2u * TILE_BYTES);
+    if (t == p.stall_tile) return;  // failure-detection test: nothing lands
     bulk_load(dst, xb + t * TILE_BYTES, TILE_BYTES, bar);
     bulk_load(dst + TILE_BYTES, yb + t * TILE_BYTES, TILE_BYTES, bar);
   };
@@ -1186,7 +1339,7 @@ __global__ void __launch_bounds__(kThreads)
   uint32_t stage = 0, phase = 0;  // k % STAGES and (k / STAGES) & 1
   uint64_t k = 0;
   for (; k < mine; ++k) {
-    const bool ok = mbar_wait(&full[stage], phase);
+    const bool ok = mbar_wait(&full[stage], phase, p.wait_cycles);
     const uint32_t *xs = reinterpret_cast<const uint32_t *>(ring + stage * (2 * TILE_BYTES));
     const uint32_t *ys = xs + shape::TILE_WORDS;
 #pragma unroll
@@ -1242,16 +1395,17 @@ __global__ void __launch_bounds__(kThreads)
     // Let the copies this block still has in flight land before it exits.
     if (threadIdx.x == 0) {
       for (uint64_t j = k; j < mine && j < k + STAGES; ++j)
-        mbar_wait(&full[j % STAGES], static_cast<uint32_t>((j / STAGES) & 1));
+        mbar_wait(&full[j % STAGES], static_cast<uint32_t>((j / STAGES) & 1),
+                  p.wait_cycles);
       atomicOr(p.status, static_cast<unsigned int>(AUT_STATUS_WAIT_TIMEOUT));
     }
     __syncthreads();
   } else {
     ragged_tail<Codec>(xb, xo, yb, yo, tiles * shape::TILE_VALUES, p.n, acc, smem);
   }
-  const double mine_sum = failed ? __longlong_as_double(0x7ff8000000000000ll) : acc.value();
-  const double s = block_sum(mine_sum, scratch);
-  grid_finish(s, p.partials + static_cast<uint64_t>(batch) * gridDim.x,
+  const dd mine_sum = failed ? dd{__longlong_as_double(0x7ff8000000000000ll), 0.0} : acc.pair();
+  const dd s = block_sum_dd(mine_sum, scratch);
+  grid_finish_dd(s, p.partials + 2 * static_cast<uint64_t>(batch) * gridDim.x,
               p.tickets + batch, p.results + batch, scratch);
 }
 
@@ -1741,8 +1895,8 @@ int auto_strategy(int32_t format, int32_t layout, int32_t accum) {
 // Decoders per format (the reference's decoder_kind axis): the E8 formats,
 // raw storage and e2m3 decode DIRECT (bit moves / hardware conversion);
 // lns8_r3 has FULL_LUT and FUSED_SUM_LUT; lns16_r11 has FULL_LUT (FP32
-// only: the table is 128 KiB of FP32), FRACTION_LUT and FRACTION_LUT_FUSED.
-// AUTO picks the fastest measured one.
+// only: the table is 128 KiB of FP32), FRACTION_LUT and FRACTION_LUT_FUSED;
+// both have EX2_APPROX.  AUTO picks the fastest measured exact one.
 kernel_entry lookup(int32_t format, int32_t layout, int32_t accum, int strategy,
                     int decoder = AUT_DECODER_AUTO) {
   using namespace aut::dev;
@@ -1776,9 +1930,17 @@ kernel_entry lookup(int32_t format, int32_t layout, int32_t accum, int strategy,
     if (!lns && decoder != AUT_DECODER_DIRECT) return {};
     if (lns && decoder == AUT_DECODER_DIRECT) return {};
     if (format == AUT_FMT_LNS8_R3 && decoder != AUT_DECODER_FULL_LUT &&
-        decoder != AUT_DECODER_FUSED_SUM_LUT)
+        decoder != AUT_DECODER_FUSED_SUM_LUT && decoder != AUT_DECODER_EX2_APPROX)
       return {};
     if (format == AUT_FMT_LNS16_R11 && decoder == AUT_DECODER_FUSED_SUM_LUT) return {};
+  }
+  if (decoder == AUT_DECODER_EX2_APPROX) {
+    // never chosen by AUTO: approximate
+    if (format == AUT_FMT_LNS8_R3)
+      return accum == AUT_ACCUM_FP32 ? make_entry<lns_ex2_codec<8, float>, acc_f32>(s, 0)
+                                     : make_entry<lns_ex2_codec<8, double>, acc_f64>(s, 0);
+    return accum == AUT_ACCUM_FP32 ? make_entry<lns_ex2_codec<16, float>, acc_f32>(s, 0)
+                                   : make_entry<lns_ex2_codec<16, double>, acc_f64>(s, 0);
   }
   if (format == AUT_FMT_LNS16_R11) {
     const bool f32 = accum == AUT_ACCUM_FP32;
@@ -1795,10 +1957,13 @@ kernel_entry lookup(int32_t format, int32_t layout, int32_t accum, int strategy,
     }
   }
   switch (format) {
-  case AUT_FMT_FP32: return pick<e8_codec<32, 32>>(s, accum, 0);
+  // raw storage: accumulation compensated per product (acc_f32c, acc_f64c)
+  case AUT_FMT_FP32:
+    return accum == AUT_ACCUM_FP32 ? make_entry<e8_codec<32, 32>, acc_f32c>(s, 0)
+                                   : make_entry<e8_codec<32, 32>, acc_f64c>(s, 0);
   case AUT_FMT_FP64:
     if (accum != AUT_ACCUM_FP64) return {};
-    return make_entry<f64_codec, acc_f64>(s, 0);
+    return make_entry<f64_codec, acc_f64c>(s, 0);
   case AUT_FMT_E2M3:
     return dense ? pick<e2m3_codec<6>>(s, accum, 0) : pick<e2m3_codec<8>>(s, accum, 0);
   case AUT_FMT_E8M0:
@@ -1909,6 +2074,8 @@ static aut::dev::dot_params params_for(const void *x, const void *y, uint64_t n,
   p.y_index_stride = bl.y_index_stride;
   p.n = n;
   p.vector_ok = aligned ? 1 : 0;
+  p.wait_cycles = aut::kWaitCyclesDefault;
+  p.stall_tile = ~0ull;
   return p;
 }
 
@@ -1990,6 +2157,8 @@ aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
     p.tickets = tickets;
     p.results = results + b0;
     p.status = status;
+    p.wait_cycles = ws->wait_cycles;
+    p.stall_tile = ws->stall_tile;
     dim3 grid(static_cast<unsigned>(per_pair), nb);
     e.fn<<<grid, aut::dev::kThreads, e.smem, static_cast<cudaStream_t>(stream)>>>(p);
     AUT_CUDA_TRY(cudaGetLastError());
@@ -2123,13 +2292,15 @@ aut_status gemv_launch(aut_workspace *ws, int32_t format, int32_t layout, int32_
 // Same launch as dot_launch for callers that bring their own reduction
 // scratch and have no workspace: formats that need decode tables (LNS) are
 // refused, the grid never uses more than `slots` partial slots in total, and
-// nothing is allocated.
+// nothing is allocated.  Once the format is accepted, `clear_bytes` bytes at
+// `clear` (the counters) are zeroed on the stream before the launch; a
+// refused call enqueues nothing.
 aut_status dot_launch_scratch(int sm_count, int32_t format, int32_t layout,
                               int32_t accum, const void *x, const void *y,
                               uint64_t n, uint32_t batch, const batch_layout &bl,
                               double *results, void *stream, double *partials,
                               unsigned int *tickets, unsigned int *status,
-                              int slots) {
+                              int slots, void *clear, size_t clear_bytes) {
   kernel_entry e = lookup(format, layout, accum, AUT_STRATEGY_AUTO);
   if (e.fn == nullptr)
     return fail(AUT_ERR_UNSUPPORTED,
@@ -2149,7 +2320,7 @@ aut_status dot_launch_scratch(int sm_count, int32_t format, int32_t layout,
   if (wanted == 0) wanted = 1;
   int per_pair = (sm_count * e.blocks_per_sm + static_cast<int>(batch) - 1) /
                  static_cast<int>(batch);
-  const int cap = slots / static_cast<int>(batch);
+  const int cap = slots / (2 * static_cast<int>(batch));  // two slots per block
   if (per_pair > cap) per_pair = cap;
   if (static_cast<uint64_t>(per_pair) > wanted) per_pair = static_cast<int>(wanted);
   if (per_pair < 1) per_pair = 1;
@@ -2160,6 +2331,8 @@ aut_status dot_launch_scratch(int sm_count, int32_t format, int32_t layout,
   p.tickets = tickets;
   p.results = results;
   p.status = status;
+  if (clear_bytes > 0)
+    AUT_CUDA_TRY(cudaMemsetAsync(clear, 0, clear_bytes, static_cast<cudaStream_t>(stream)));
   dim3 grid(static_cast<unsigned>(per_pair), batch);
   e.fn<<<grid, aut::dev::kThreads, e.smem, static_cast<cudaStream_t>(stream)>>>(p);
   AUT_CUDA_TRY(cudaGetLastError());

@@ -86,6 +86,37 @@ __device__ __forceinline__ uint32_t load_code(const unsigned char *base,
   }
 }
 
+// ---- double-double arithmetic ------------------------------------------------
+// A sum carried as hi + lo with |lo| <= ulp(hi) / 2: the per-thread partials
+// of the FP64 accumulators and every step of the block and grid reductions,
+// so the reductions add no rounding of their own and the DOT is rounded
+// once at the end.  Explicit _rn intrinsics keep the compiler from fusing
+// the error terms into FMAs.
+struct dd {
+  double hi, lo;
+};
+
+// s + e = a + b exactly (Knuth's two-sum).
+__device__ __forceinline__ void two_sum(double a, double b, double &s, double &e) {
+  s = __dadd_rn(a, b);
+  const double bb = __dsub_rn(s, a);
+  e = __dadd_rn(__dsub_rn(a, __dsub_rn(s, bb)), __dsub_rn(b, bb));
+}
+
+// An inf or NaN high part stays inf or NaN whatever is added to it, so its
+// low part (then inf - inf or NaN) carries nothing and is dropped: inf and
+// NaN pass through the reductions as a plain sum would give them.
+__device__ __forceinline__ dd dd_add(dd a, dd b) {
+  double s, e;
+  two_sum(a.hi, b.hi, s, e);
+  if (!isfinite(s)) return {s, 0.0};
+  e = __dadd_rn(e, __dadd_rn(a.lo, b.lo));
+  dd r;
+  two_sum(s, e, r.hi, r.lo);
+  if (!isfinite(r.hi)) r.lo = 0.0;  // s + e overflowed
+  return r;
+}
+
 // ---- per-thread accumulators -------------------------------------------------
 // FP32: four independent FMA chains, carried into FP64 at every flush().
 struct acc_f32 {
@@ -107,9 +138,55 @@ struct acc_f32 {
     flush();
     return total;
   }
+  __device__ __forceinline__ dd pair() { return {value(), 0.0}; }
 };
 
-// FP64: two independent FMA chains of exactly widened operands.
+// FP32, compensated (raw FP32 storage, HBM-bound with FP32 issue to
+// spare): four FP32 chains, each product split into its rounded value and
+// exact error by one FMA, added by an FP32 two-sum whose error joins a
+// second FP32 chain; every flush carries hi + lo of each chain into an FP64
+// double-double total.  All per-product arithmetic stays FP32; the error of
+// a 32-product chain is then second order (~2^-48 relative), so the DOT is
+// close to the exact sum rounded once.
+struct acc_f32c {
+  float hi[4] = {0.f, 0.f, 0.f, 0.f};
+  float lo[4] = {0.f, 0.f, 0.f, 0.f};
+  dd total = {0.0, 0.0};
+  __device__ __forceinline__ void mac(int slot, float x, float y) {
+    const int k = slot & 3;
+    const float p = __fmul_rn(x, y);
+    const float pe = __fmaf_rn(x, y, -p);
+    const float s = __fadd_rn(hi[k], p);
+    const float bb = __fsub_rn(s, hi[k]);
+    const float e = __fadd_rn(__fsub_rn(hi[k], __fsub_rn(s, bb)), __fsub_rn(p, bb));
+    hi[k] = s;
+    lo[k] = __fadd_rn(lo[k], __fadd_rn(e, pe));
+  }
+  __device__ __forceinline__ void mac_d(int, double x, double y) {
+    const double p = __dmul_rn(x, y);
+    total = dd_add(total, {p, __fma_rn(x, y, -p)});
+  }
+  __device__ __forceinline__ void add_exact(double v) { total = dd_add(total, {v, 0.0}); }
+  __device__ __forceinline__ void flush() {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const double h = static_cast<double>(hi[k]);
+      total = dd_add(total, {h, isfinite(h) ? static_cast<double>(lo[k]) : 0.0});
+      hi[k] = lo[k] = 0.f;
+    }
+  }
+  __device__ __forceinline__ dd pair() {
+    flush();
+    return total;
+  }
+  __device__ __forceinline__ double value() {
+    const dd r = pair();
+    return r.hi + r.lo;
+  }
+};
+
+// FP64: two independent FMA chains of exactly widened operands, joined
+// without rounding for the double-double reductions.
 struct acc_f64 {
   double a[2] = {0.0, 0.0};
   __device__ __forceinline__ void mac(int slot, float x, float y) {
@@ -121,42 +198,93 @@ struct acc_f64 {
   __device__ __forceinline__ void add_exact(double v) { a[0] += v; }
   __device__ __forceinline__ void flush() {}
   __device__ __forceinline__ double value() { return a[0] + a[1]; }
+  __device__ __forceinline__ dd pair() { return dd_add({a[0], 0.0}, {a[1], 0.0}); }
 };
 
-// ---- block / grid reduction (deterministic) ------------------------------------
+// FP64, compensated per product (raw FP32 / FP64 storage, whose DOTs are
+// HBM-bound with FP64 issue to spare): each product is split into its
+// rounded value and exact error (exact already for FP32 operands; one FMA
+// for FP64 ones), added by two-sum, and every rounding error is carried in
+// lo.  The thread's sum is hi + lo to about 2^-100 relative, so the DOT is
+// close to the exact sum rounded once.
+struct acc_f64c {
+  double hi[2] = {0.0, 0.0};
+  double lo[2] = {0.0, 0.0};
+  __device__ __forceinline__ void add(int k, double p, double pe) {
+    double e;
+    two_sum(hi[k], p, hi[k], e);
+    lo[k] = __dadd_rn(lo[k], __dadd_rn(e, pe));
+  }
+  __device__ __forceinline__ void mac(int slot, float x, float y) {
+    add(slot & 1, __dmul_rn(static_cast<double>(x), static_cast<double>(y)), 0.0);
+  }
+  __device__ __forceinline__ void mac_d(int slot, double x, double y) {
+    const double p = __dmul_rn(x, y);
+    add(slot & 1, p, __fma_rn(x, y, -p));
+  }
+  __device__ __forceinline__ void add_exact(double v) { add(0, v, 0.0); }
+  __device__ __forceinline__ void flush() {}
+  __device__ __forceinline__ dd pair() {
+    return dd_add({hi[0], isfinite(hi[0]) ? lo[0] : 0.0},
+                  {hi[1], isfinite(hi[1]) ? lo[1] : 0.0});
+  }
+  __device__ __forceinline__ double value() {
+    const dd r = pair();
+    return r.hi + r.lo;
+  }
+};
+
+// ---- block / grid reduction (deterministic, double-double) ---------------------
 __device__ __forceinline__ double warp_sum(double v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
 
+__device__ __forceinline__ dd warp_sum_dd(dd v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const dd w = {__shfl_down_sync(0xffffffffu, v.hi, o),
+                  __shfl_down_sync(0xffffffffu, v.lo, o)};
+    v = dd_add(v, w);
+  }
+  return v;  // valid in lane 0
+}
+
+// Words of shared scratch the block reduction needs.
+constexpr int kScratchDoubles = 2 * (kThreads / 32);
+
 // Sum over the block; the result is valid in thread 0.
-__device__ __forceinline__ double block_sum(double v, double *scratch) {
-  v = warp_sum(v);
+__device__ __forceinline__ dd block_sum_dd(dd v, double *scratch) {
+  v = warp_sum_dd(v);
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  if (lane == 0) scratch[warp] = v;
+  if (lane == 0) {
+    scratch[2 * warp] = v.hi;
+    scratch[2 * warp + 1] = v.lo;
+  }
   __syncthreads();
-  double s = 0.0;
+  dd s = {0.0, 0.0};
   if (warp == 0) {
-    s = lane < (kThreads / 32) ? scratch[lane] : 0.0;
-    s = warp_sum(s);
+    if (lane < kThreads / 32) s = {scratch[2 * lane], scratch[2 * lane + 1]};
+    s = warp_sum_dd(s);
   }
   __syncthreads();
   return s;
 }
 
-// Single-pass grid reduction: every block publishes its partial, the last
-// block to arrive (atomic ticket after a fence) sums the partials in block
-// order and resets the ticket for the next launch.  No block waits on
-// another, so the pattern cannot hang.
-__device__ __forceinline__ void grid_finish(double block_partial,
-                                            double *partials,
-                                            unsigned int *ticket,
-                                            double *result, double *scratch) {
+// Single-pass grid reduction: every block publishes its partial (hi, lo at
+// partials[2b], [2b + 1]), the last block to arrive (atomic ticket after a
+// fence) sums the partials in block order and resets the ticket for the next
+// launch.  No block waits on another, so the pattern cannot hang.  The
+// result is hi + lo rounded once.
+__device__ __forceinline__ void grid_finish_dd(dd block_partial, double *partials,
+                                               unsigned int *ticket, double *result,
+                                               double *scratch) {
   __shared__ bool last_block;
   if (threadIdx.x == 0) {
-    partials[blockIdx.x] = block_partial;
+    partials[2 * blockIdx.x] = block_partial.hi;
+    partials[2 * blockIdx.x + 1] = block_partial.lo;
     __threadfence();
     const unsigned int arrived = atomicAdd(ticket, 1u);
     last_block = (arrived == gridDim.x - 1);
@@ -164,12 +292,12 @@ __device__ __forceinline__ void grid_finish(double block_partial,
   __syncthreads();
   if (!last_block) return;
   __threadfence();
-  double s = 0.0;
+  dd s = {0.0, 0.0};
   for (unsigned int b = threadIdx.x; b < gridDim.x; b += kThreads)
-    s += __ldcg(partials + b);
-  s = block_sum(s, scratch);
+    s = dd_add(s, {__ldcg(partials + 2 * b), __ldcg(partials + 2 * b + 1)});
+  s = block_sum_dd(s, scratch);
   if (threadIdx.x == 0) {
-    *result = s;
+    *result = __dadd_rn(s.hi, s.lo);
     *ticket = 0u;
   }
 }

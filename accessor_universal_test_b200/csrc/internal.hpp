@@ -10,6 +10,11 @@
 #include <mutex>
 #include <string>
 
+namespace aut {
+// Bound of the bulk-copy kernels' barrier waits: ~2 s of SM clock at 2 GHz.
+constexpr long long kWaitCyclesDefault = 4000000000LL;
+} // namespace aut
+
 namespace aut::lib {
 
 // ---- registry ---------------------------------------------------------------
@@ -89,6 +94,9 @@ struct aut_workspace {
   unsigned int *tickets = nullptr; // [kMaxBatchPerLaunch + 1], kept at zero;
                                    // the last word is the sticky status
   std::mutex mutex;
+  // failure-detection test hook (aut_workspace_inject_stall)
+  long long wait_cycles = aut::kWaitCyclesDefault;
+  uint64_t stall_tile = ~0ull;
   int table_ids[aut::lib::kTableFormatsCached];
   aut_workspace() {
     for (int &id : table_ids) id = -1;

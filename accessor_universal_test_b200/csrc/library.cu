@@ -567,6 +567,18 @@ aut_status aut_workspace_status(aut_workspace *ws, uint32_t *status,
   return AUT_OK;
 }
 
+aut_status aut_workspace_inject_stall(aut_workspace *ws, uint64_t stall_tile,
+                                      uint64_t wait_cycles) {
+  clear_error();
+  if (ws == nullptr) return fail(AUT_ERR_INVALID_ARGUMENT, "workspace is NULL");
+  if (wait_cycles > static_cast<uint64_t>(aut::kWaitCyclesDefault))
+    return fail(AUT_ERR_INVALID_ARGUMENT, "wait_cycles above the default bound");
+  ws->stall_tile = stall_tile;
+  ws->wait_cycles = wait_cycles == 0 ? aut::kWaitCyclesDefault
+                                     : static_cast<long long>(wait_cycles);
+  return AUT_OK;
+}
+
 static aut_status check_dot_args(aut_workspace *ws, int32_t format,
                                  int32_t layout, int32_t accum, const void *x,
                                  const void *y, uint64_t n, const double *res) {
@@ -610,7 +622,7 @@ aut_status aut_dot_variant(aut_workspace *ws, int32_t format, int32_t layout,
   if (st != AUT_OK) return st;
   if (strategy < AUT_STRATEGY_AUTO || strategy > AUT_STRATEGY_SCALAR)
     return fail(AUT_ERR_INVALID_ARGUMENT, "unknown access strategy");
-  if (decoder < AUT_DECODER_AUTO || decoder > AUT_DECODER_FUSED_SUM_LUT)
+  if (decoder < AUT_DECODER_AUTO || decoder > AUT_DECODER_EX2_APPROX)
     return fail(AUT_ERR_INVALID_ARGUMENT, "unknown decoder");
   device_scope scope(ws->device);
   AUT_CUDA_TRY(scope.err);
@@ -651,7 +663,7 @@ aut_status aut_gemv(aut_workspace *ws, int32_t format, int32_t layout,
   if (st != AUT_OK) return st;
   if (strategy < AUT_STRATEGY_AUTO || strategy > AUT_STRATEGY_SCALAR)
     return fail(AUT_ERR_INVALID_ARGUMENT, "unknown access strategy");
-  if (decoder < AUT_DECODER_AUTO || decoder > AUT_DECODER_FUSED_SUM_LUT)
+  if (decoder < AUT_DECODER_AUTO || decoder > AUT_DECODER_EX2_APPROX)
     return fail(AUT_ERR_INVALID_ARGUMENT, "unknown decoder");
   if (rows == 0) return AUT_OK;
   if (rows > 0xffffffffull)

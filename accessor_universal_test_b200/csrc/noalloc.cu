@@ -22,7 +22,14 @@
 //     (one stream, or events);
 //   * the first call on each device looks up the array's device address
 //     (cudaGetSymbolAddress, which also loads the module if it is not loaded
-//     yet); make that first call before any stream capture;
+//     yet); make that first call before any stream capture.  Only a
+//     successful lookup is kept: a call whose lookup failed returns
+//     AUT_ERR_CUDA and the next call on that device tries again;
+//   * there is no status query: a DOT whose bounded bulk-copy wait gave up
+//     (AUT_STATUS_WAIT_TIMEOUT under aut_dot) shows up only as NaN in its
+//     results[b];
+//   * a call refused for its arguments or format touches nothing on the
+//     device;
 //   * nothing here calls cudaMalloc, cudaFree or an allocating library.
 #include "dot_device.cuh"
 #include "internal.hpp"
@@ -34,7 +41,7 @@
 
 namespace {
 
-constexpr int kSlots = 4096;     // FP64 partials, one per block of a call
+constexpr int kSlots = 4096;     // FP64 words of partials, two per block of a call
 constexpr int kMaxPairs = 64;    // DOTs per call
 constexpr int kMaxDevices = 64;
 
@@ -51,23 +58,30 @@ static __device__ __align__(256) unsigned char
     noalloc_scratch[sizeof(scratch_layout)];
 
 struct device_setup {
-  std::once_flag once;
-  cudaError_t err = cudaSuccess;
+  std::mutex mutex;
   scratch_layout *scratch = nullptr;  // device address of noalloc_scratch
   int sm_count = 0;
   int major = 0;
 };
 device_setup setups[kMaxDevices];
 
-// Runs once per device, with that device current.
-void set_up(device_setup &s, int device) {
+// Looks the array up on `device` (current) until a lookup succeeds; the
+// result is published only when every query succeeded.
+cudaError_t set_up(device_setup &s, int device) {
+  std::lock_guard<std::mutex> lock(s.mutex);
+  if (s.scratch != nullptr) return cudaSuccess;
   void *ptr = nullptr;
-  s.err = cudaGetSymbolAddress(&ptr, noalloc_scratch);
-  if (s.err != cudaSuccess) return;
+  int sm_count = 0, major = 0;
+  cudaError_t err = cudaGetSymbolAddress(&ptr, noalloc_scratch);
+  if (err == cudaSuccess)
+    err = cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, device);
+  if (err == cudaSuccess)
+    err = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+  if (err != cudaSuccess) return err;
+  s.sm_count = sm_count;
+  s.major = major;
   s.scratch = static_cast<scratch_layout *>(ptr);
-  s.err = cudaDeviceGetAttribute(&s.sm_count, cudaDevAttrMultiProcessorCount, device);
-  if (s.err != cudaSuccess) return;
-  s.err = cudaDeviceGetAttribute(&s.major, cudaDevAttrComputeCapabilityMajor, device);
+  return cudaSuccess;
 }
 
 } // namespace
@@ -78,7 +92,7 @@ aut_status dot_launch_scratch(int sm_count, int32_t format, int32_t layout,
                               uint64_t n, uint32_t batch, const batch_layout &bl,
                               double *results, void *stream, double *partials,
                               unsigned int *tickets, unsigned int *status,
-                              int slots);
+                              int slots, void *clear, size_t clear_bytes);
 }
 
 extern "C" aut_status aut_dot_noalloc(int32_t format, int32_t layout,
@@ -99,7 +113,7 @@ extern "C" aut_status aut_dot_noalloc(int32_t format, int32_t layout,
   if (batch > static_cast<uint32_t>(kMaxPairs))
     return fail(AUT_ERR_TOO_LARGE,
                 "aut_dot_noalloc runs at most 64 DOTs per call (its scratch holds "
-                "4096 partial slots and 64 counters); split the batch or use "
+                "2048 block partials and 64 counters); split the batch or use "
                 "aut_dot_batched");
   if (n > 0 && (x == nullptr || y == nullptr))
     return fail(AUT_ERR_INVALID_ARGUMENT, "x or y is NULL");
@@ -111,20 +125,20 @@ extern "C" aut_status aut_dot_noalloc(int32_t format, int32_t layout,
   if (device < 0 || device >= kMaxDevices)
     return fail(AUT_ERR_INVALID_ARGUMENT, "device index beyond the set-up table");
   device_setup &s = setups[device];
-  std::call_once(s.once, set_up, std::ref(s), device);
-  if (s.err != cudaSuccess) return cuda_fail(s.err, "aut_dot_noalloc set-up");
+  const cudaError_t err = set_up(s, device);
+  if (err != cudaSuccess) return cuda_fail(err, "aut_dot_noalloc set-up");
   if (s.major != 10)
     return fail(AUT_ERR_NO_DEVICE, "libautdot is built for sm_100a");
 
-  // The counters must start at zero; a call that never finished (launch
-  // error, killed context) could have left them otherwise.
-  AUT_CUDA_TRY(cudaMemsetAsync(s.scratch->tickets, 0,
-                               sizeof(s.scratch->tickets) + sizeof(s.scratch->status),
-                               static_cast<cudaStream_t>(stream)));
+  // The counters and the status word are cleared on the caller's stream
+  // right before the launch (once the format has been accepted): a call that
+  // never finished (launch error, killed context) could have left them
+  // non-zero.
   batch_layout bl;
   bl.x_stride = bl.y_stride = batch_stride_bytes;
   return dot_launch_scratch(s.sm_count, format, layout, accum, x, y, n, batch,
                             bl, results, stream,
                             s.scratch->partials, s.scratch->tickets,
-                            &s.scratch->status, kSlots);
+                            &s.scratch->status, kSlots, s.scratch->tickets,
+                            sizeof(s.scratch->tickets) + sizeof(s.scratch->status));
 }

@@ -13,14 +13,21 @@ crossing word boundaries, N = 2^27 values per GPU, x, y uniform[-1, 1)
 A step is one fused DOT per format (six launches) plus, on more than one GPU,
 one NCCL all-reduce of the six FP64 partials.
 
-value    packed HBM GB/s of the whole job (2 N bits / 8 per DOT, all GPUs),
-         inputs resident in HBM; each pair is larger than the 126 MB L2 and
-         consecutive DOTs read different buffers, so no L2 flush is needed.
-e2e      the same metric through the C ABI from pinned HOST buffers: every
-         step copies the packed vectors host->device, runs the DOTs and reads
-         the FP64 results back.
-roofline the dominant kernel's packed bytes per launch / its CUDA-event
-         launch time, against the measured HBM copy bandwidth.
+value       packed HBM GB/s of the whole job (2 N bits / 8 per DOT, all GPUs),
+            inputs resident in HBM; each pair is larger than the 126 MB L2 and
+            consecutive DOTs read different buffers, so no L2 flush is needed.
+e2e         the same metric through the C ABI from pinned HOST buffers: every
+            step copies the packed vectors host->device, runs the DOTs and
+            reads the FP64 results back.
+roofline    the dominant kernel's packed bytes per launch / its CUDA-event
+            launch time, against the measured HBM copy bandwidth.
+per_config  (one GPU) every other storage format of the benchmark's
+            configurations at its stated size -- raw FP32/FP64 (with the
+            N = 2^10 ... 2^27 sweep), e2m3 dense and padded, the E8 sweep with
+            the FP64 accumulator, lns8_r3 / lns16_r11 on the cancellation
+            pair -- each accumulator and decoder: CUDA-event GB/s, fraction of
+            the measured peak, and the normalised error against the
+            reference's compensated long-double CPU DOT.
 
 The gemv workload runs aut_gemv instead: a 1024-row matrix of the E8 sweep
 formats with N / 1024 columns per GPU (rows sharded over GPUs, no
@@ -43,26 +50,55 @@ sys.path.insert(0, HERE)
 N_DEFAULT = 1 << 27
 SEED = 0x243F6A8885A308D3
 HBM_FALLBACK_GBS = 6650.0
+DENSE, PADDED = 0, 1
+
+# (family, total bits, exponent bits / LNS fraction bits, finite) of the
+# formats the benchmark uses -- the registry entries of storage_formats.hpp
+# and lns_benchmark_core.hpp, kept here so that the reference arm needs no
+# product library.
+FORMAT_DESC = {
+    "fp32": (3, 32, 8, 0), "fp64": (4, 64, 11, 0), "e2m3": (0, 6, 2, 1),
+    "e8m0": (0, 9, 8, 0), "e8m1": (0, 10, 8, 0), "e8m3": (0, 12, 8, 0),
+    "e8m5": (0, 14, 8, 0), "bf16_e8m7": (0, 16, 8, 0), "e8m15": (0, 24, 8, 0),
+    "lns8_r3": (2, 8, 3, 0), "lns16_r11": (2, 16, 11, 0),
+}
+E8_SWEEP = [("e8m0", 0), ("e8m1", 0), ("e8m3", 0), ("e8m5", 0), ("bf16_e8m7", 0),
+            ("e8m15", 0)]
 
 WORKLOADS = {
     # name: (description, [(format, generator kind)], layout, n per GPU)
     "e8-sweep": ("E8 truncated-float bit-width sweep e8m0/e8m1/e8m3/e8m5/bf16_e8m7/e8m15 "
                  "(9/10/12/14/16/24 bits), dense LSB-first u32 bitstream, x,y uniform[-1,1)",
-                 [("e8m0", 0), ("e8m1", 0), ("e8m3", 0), ("e8m5", 0), ("bf16_e8m7", 0),
-                  ("e8m15", 0)], 0, N_DEFAULT),
+                 E8_SWEEP, DENSE, N_DEFAULT),
     "e2m3": ("FP6 E2M3 dense (4 values per 24 bits), x,y ~ N(0,1) (Irwin-Hall), RNE encoded",
-             [("e2m3", 2)], 0, N_DEFAULT),
+             [("e2m3", 2)], DENSE, N_DEFAULT),
     "lns": ("LNS lns8_r3 and lns16_r11, N=2^28, cancellation pair y_i = s_i x_i (1+1e-6 u_i)",
-            [("lns8_r3", 3), ("lns16_r11", 3)], 0, 1 << 28),
+            [("lns8_r3", 3), ("lns16_r11", 3)], DENSE, 1 << 28),
     "raw": ("raw FP32 and FP64 storage DOT, x,y uniform[-1,1)",
-            [("fp32", 1), ("fp64", 0)], 0, N_DEFAULT),
+            [("fp32", 1), ("fp64", 0)], DENSE, N_DEFAULT),
     "gemv": ("GEMV over the E8 sweep formats: 1024 x N/1024 matrix per GPU times a dense "
-             "vector of the same format, uniform[-1,1)",
-             [("e8m0", 0), ("e8m1", 0), ("e8m3", 0), ("e8m5", 0), ("bf16_e8m7", 0),
-              ("e8m15", 0)], 0, N_DEFAULT),
+             "vector of the same format, uniform[-1,1)", E8_SWEEP, DENSE, N_DEFAULT),
 }
 GEMV_ROWS = 1024
 METRIC = "decoded elems/s & HBM GB/s (% of 8 TB/s) at N=2^27/GPU, 1-8 GPUs; normalized err"
+
+DECODERS = {"auto": 0, "direct": 1, "full_lut": 2, "fraction_lut": 3,
+            "fraction_lut_fused": 4, "fused_sum_lut": 5, "ex2_approx": 6}
+
+# The other configurations, timed on one GPU after the headline:
+# (group, format, generator kind, layout, n, accumulators, decoders)
+PER_CONFIG = [
+    ("raw", "fp32", 1, DENSE, 1 << 27, ("fp32", "fp64"), ("auto",)),
+    ("raw", "fp64", 0, DENSE, 1 << 27, ("fp64",), ("auto",)),
+    ("e2m3", "e2m3", 2, DENSE, 1 << 27, ("fp32", "fp64"), ("auto", "full_lut")),
+    ("e2m3", "e2m3", 2, PADDED, 1 << 27, ("fp32", "fp64"), ("auto",)),
+] + [("e8-sweep", f, k, DENSE, 1 << 27, ("fp64",), ("auto",)) for f, k in E8_SWEEP] + [
+    ("lns", "lns8_r3", 3, DENSE, 1 << 28, ("fp32", "fp64"),
+     ("auto", "full_lut", "fused_sum_lut", "ex2_approx")),
+    ("lns", "lns16_r11", 3, DENSE, 1 << 28, ("fp32", "fp64"),
+     ("auto", "fraction_lut_fused", "fraction_lut", "full_lut", "ex2_approx")),
+]
+RAW_SWEEP = [10, 16, 20, 23, 26, 27]
 
 
 def parse():
@@ -76,6 +112,8 @@ def parse():
     p.add_argument("--strategy", choices=["auto", "ldg", "tma"], default="auto")
     p.add_argument("--n", type=int, default=0, help="values per GPU (default: workload's)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-per-config", action="store_true",
+                   help="skip the other configurations (one GPU only)")
     p.add_argument("--e2e-steps", type=int, default=6)
     return p.parse_args()
 
@@ -125,7 +163,8 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
-            # the timed region starts once nvidia-smi reports (it needs ~0.1 s)
+            # wait for the first sample (nvidia-smi needs ~0.1 s to start)
+            # before the ranks meet at the barrier that opens the timed region
             t0 = time.time()
             while not self.lines and time.time() - t0 < 5.0 and self.proc.poll() is None:
                 time.sleep(0.01)
@@ -181,14 +220,17 @@ def physical_gpu(local: int) -> int:
 
 
 # ---- CPU baseline (the reference's CPU path on the host cores) -------------------
+def _pyoracle():
+    sys.path.insert(0, os.path.join(HERE, "oracle"))
+    import pyoracle
+    return pyoracle
+
+
 def cpu_reference_dot(fmt_name, stride, xw, yw, n, threads):
     """The reference's host decode + compensated long-double DOT; oracle/_ref
     when the reference was compiled here, else the oracle's restatement."""
-    sys.path.insert(0, os.path.join(HERE, "oracle"))
-    import pyoracle
-    ref = None
-    if os.path.exists(pyoracle.REF_SO):
-        ref = pyoracle.Reference()
+    pyoracle = _pyoracle()
+    ref = pyoracle.reference()
     if ref is not None and fmt_name in ref.formats:
         d, s = ref.dot_dense(fmt_name, stride, xw, yw, n, threads)
         return d, s, "reference"
@@ -198,9 +240,7 @@ def cpu_reference_dot(fmt_name, stride, xw, yw, n, threads):
         d, s = ref.dot_raw(xw.view(dt)[:n], yw.view(dt)[:n], threads)
         return d, s, "reference"
     orc = pyoracle.oracle()
-    from accessor_universal_test_b200 import _lib
-    desc = _lib.format_info(_lib.format_id(fmt_name))
-    d, s = orc.dot_dense(desc, stride, xw, yw, n, threads)
+    d, s = orc.dot_dense(FORMAT_DESC[fmt_name], stride, xw, yw, n, threads)
     return d, s, "port"
 
 
@@ -211,56 +251,78 @@ def host_threads():
         return os.cpu_count() or 1
 
 
+def normalized_error(got, d, s):
+    import numpy as np
+    ref = np.longdouble(d[0]) + np.longdouble(d[1])
+    sabs = np.longdouble(s[0]) + np.longdouble(s[1])
+    if got != got:
+        return float("nan")
+    return float(abs(np.longdouble(got) - ref) / sabs) if sabs else 0.0
+
+
+def condition_number(d, s):
+    import numpy as np
+    ref = abs(np.longdouble(d[0]) + np.longdouble(d[1]))
+    sabs = np.longdouble(s[0]) + np.longdouble(s[1])
+    return float(sabs / ref) if ref else float("inf")
+
+
 # ---- the reference arm ---------------------------------------------------------
 def run_reference_arm(args, rank, world):
+    """The reference's own CPU implementation of the path (host decode +
+    compensated long-double DOT, compiled from its headers into
+    oracle/_ref/libautref.so), on rank 0 with every host thread.  Inputs are
+    generated by the oracle's generators and encoded and packed by the
+    reference's own host codec; nothing here loads the product library."""
     if rank != 0:
         return 0
     import numpy as np
     desc, fmts, layout, n_full = WORKLOADS[args.workload]
-    from accessor_universal_test_b200 import _lib
     threads = host_threads()
-    # Encoded inputs come from the product's host codec (no GPU needed here).
-    rng_n = 1 << 22
-    streams = []
-    sys.path.insert(0, os.path.join(HERE, "oracle"))
-    import pyoracle
+    pyoracle = _pyoracle()
     orc = pyoracle.oracle()
+    ref = pyoracle.reference()
+    kind_used = "reference" if ref is not None else "port"
+    pool_n = 1 << 22  # values generated per format; every step reads a prefix
+    streams = []
     for name, kind in fmts:
-        fid = _lib.format_id(name)
-        fam, bits, _, _ = _lib.format_info(fid)
-        x = orc.synthetic(kind, SEED, 0, rng_n)
-        y = orc.synthetic(kind, SEED, 1, rng_n)
-        if fam == _lib.FAMILY_RAW_FP64:
+        fam, bits, _, _ = FORMAT_DESC[name]
+        x = orc.synthetic(kind, SEED, 0, pool_n)
+        y = orc.synthetic(kind, SEED, 1, pool_n)
+        if fam == 4:  # raw FP64
             streams.append((name, 64, x.view(np.uint32), y.view(np.uint32), bits))
+            continue
+        if fam == 3:  # raw FP32
+            streams.append((name, 32, x.astype(np.float32).view(np.uint32),
+                            y.astype(np.float32).view(np.uint32), bits))
             continue
         out = []
         for v in (x, y):
-            codes = np.empty(rng_n, np.uint32)
-            _lib.check(_lib.load().aut_encode_host(fid, v.ctypes.data, rng_n, codes.ctypes.data))
-            packed = np.zeros(_lib.storage_bytes(fid, layout, rng_n), np.uint8)
-            _lib.check(_lib.load().aut_pack_host(fid, layout, codes.ctypes.data, rng_n,
-                                                 packed.ctypes.data))
-            out.append(packed.view(np.uint32))
+            if ref is not None:
+                out.append(ref.pack_dense(bits, ref.encode(name, v)))
+            else:
+                out.append(orc.pack_dense(bits, orc.encode(FORMAT_DESC[name], v)))
         streams.append((name, bits, out[0], out[1], bits))
 
     def one_step(m):
-        kind_used = None
         for name, stride, xw, yw, _ in streams:
-            _, _, kind_used = cpu_reference_dot(name, stride, xw, yw, m, threads)
-        return kind_used
+            cpu_reference_dot(name, stride, xw, yw, m, threads)
 
-    # size the per-step sample so that the whole run stays within ~2 minutes
+    # A fixed per-step sample (the largest power of two up to 2^22 values per
+    # format for which the whole run stays within about two minutes), so that
+    # the figure is a property of the host, not of the step count.
     t0 = time.perf_counter()
-    one_step(1 << 16)
-    per_value = (time.perf_counter() - t0) / (1 << 16)
+    one_step(1 << 18)
+    per_value = (time.perf_counter() - t0) / (1 << 18)
     budget = 120.0 / max(1, args.steps + args.warmup)
-    m = int(min(rng_n, max(1 << 12, budget / max(per_value, 1e-12))))
+    m = pool_n
+    while m > (1 << 14) and m * per_value > budget:
+        m //= 2
     for _ in range(args.warmup):
         one_step(m)
     t0 = time.perf_counter()
-    kind = None
     for _ in range(args.steps):
-        kind = one_step(m)
+        one_step(m)
     elapsed = time.perf_counter() - t0
     bytes_step = sum(2 * m * b / 8 for (_, _, _, _, b) in streams)
     gbs = bytes_step * args.steps / elapsed / 1e9
@@ -269,9 +331,9 @@ def run_reference_arm(args, rank, world):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f80 (long double)",
-        "data": "synthetic",
-        "config": config_of(args, world, desc, n_full),
-        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": kind,
+        "data": "synthetic (seeded splitmix64; encoded by the reference's host codec)",
+        "config": dict(config_of(args, world, desc, n_full), sample_values_per_format=m),
+        "cpu_baseline": {"value": gbs, "unit": "GB/s", "cores": threads, "kind": kind_used,
                          "sample": f"{m} values per format per step ({len(streams)} formats), "
                                    f"host decode + compensated long-double DOT"},
         "e2e": {"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -295,6 +357,89 @@ def config_of(args, world, desc, n_full):
             "layout": "dense", "accumulator": args.accum,
             "l2": "inputs larger than L2 (every pair > 126 MB; consecutive DOTs read different buffers)",
             "parallelism": f"contiguous shards x{world}, one FP64 all-reduce per step"}
+
+
+# ---- the other configurations (one GPU) -----------------------------------------
+def run_per_config(ws, stream, threads, peak, reuse_refs):
+    """Each configuration's DOT at its stated size with every accumulator and
+    decoder: CUDA-event GB/s (inputs larger than L2 unless marked) and the
+    normalised error against the reference's CPU DOT of the same codes."""
+    import numpy as np
+    import torch
+    from accessor_universal_test_b200 import _lib, vectors
+
+    def timed(fn, reps):
+        fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps
+
+    entries = []
+    res = torch.zeros(1, dtype=torch.float64, device="cuda")
+    for group, name, kind, layout, n, accums, decoders in PER_CONFIG:
+        fid = _lib.format_id(name)
+        ws.prepare(fid)
+        fam, bits, _, _ = _lib.format_info(fid)
+        x = vectors.encoded(ws, fid, layout, kind, SEED, 0, n)
+        y = vectors.encoded(ws, fid, layout, kind, SEED, 1, n)
+        torch.cuda.synchronize()
+        stride = 64 if name == "fp64" else (bits if layout == DENSE else
+                                            (8 if bits <= 8 else 16 if bits <= 16 else 32))
+        key = (name, layout, kind, n)
+        if key in reuse_refs:
+            d, s = reuse_refs[key]
+        else:
+            d, s, _ = cpu_reference_dot(name, stride, x.cpu().numpy().view(np.uint32),
+                                        y.cpu().numpy().view(np.uint32), n, threads)
+        packed = 2 * n * bits / 8
+        for acc in accums:
+            acc_id = _lib.ACC_FP32 if acc == "fp32" else _lib.ACC_FP64
+            for dec in decoders:
+                def launch():
+                    ws.dot(fid, layout, acc_id, x.data_ptr(), y.data_ptr(), n, res.data_ptr(),
+                           stream, 0, DECODERS[dec])
+                try:
+                    t_ms = timed(launch, 20)
+                except _lib.AutError:
+                    continue  # no kernel for this decoder / accumulator
+                got = float(res.cpu()[0])
+                e = {"group": group, "format": name, "layout": "dense" if layout == DENSE
+                     else "padded", "accumulator": acc, "decoder": dec, "n": n, "ms": t_ms,
+                     "gbs": packed / (t_ms / 1e3) / 1e9,
+                     "frac_of_peak": packed / (t_ms / 1e3) / 1e9 / peak,
+                     "normalized_error": normalized_error(got, d, s)}
+                if group == "lns":
+                    e["condition_number"] = condition_number(d, s)
+                entries.append(e)
+        del x, y
+        torch.cuda.empty_cache()
+    if ws.status() != 0:
+        raise RuntimeError("a bounded device wait timed out during the configurations")
+
+    # config 2's size sweep: launch-bound to HBM-bound (small sizes stay in L2)
+    sweep = []
+    for name, kind, acc in (("fp32", 1, _lib.ACC_FP32), ("fp64", 0, _lib.ACC_FP64)):
+        fid = _lib.format_id(name)
+        bits = 64 if name == "fp64" else 32
+        for p in RAW_SWEEP:
+            n = 1 << p
+            x = vectors.encoded(ws, fid, DENSE, kind, SEED, 0, n)
+            y = vectors.encoded(ws, fid, DENSE, kind, SEED, 1, n)
+
+            def launch():
+                ws.dot(fid, DENSE, acc, x.data_ptr(), y.data_ptr(), n, res.data_ptr(), stream)
+            t_ms = timed(launch, 200 if p <= 23 else 20)
+            sweep.append({"format": name, "n": n, "ms": t_ms,
+                          "gbs": 2 * n * bits / 8 / (t_ms / 1e3) / 1e9,
+                          "l2_resident": 2 * n * bits / 8 < 126e6})
+            del x, y
+    torch.cuda.empty_cache()
+    return entries, sweep
 
 
 # ---- our arm ---------------------------------------------------------------------
@@ -385,11 +530,19 @@ def main():
         step()
     drain()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # The clock sampler is running before the ranks meet; the ranks then
+    # leave a barrier together, and on N > 1 GPUs the start event is recorded
+    # behind one more all-reduce, so that every GPU's timed region opens when
+    # that collective completes (within microseconds on all ranks) instead of
+    # whenever its host gets there.
+    sync = torch.zeros(1, dtype=torch.float64, device="cuda")
     with ClockSampler(physical_gpu(local)) as clocks:
+        if world > 1:
+            dist.barrier()
         torch.cuda.synchronize()
+        if world > 1:
+            dist.all_reduce(sync)
         clocks.mark()
         start.record()
         for _ in range(args.steps):
@@ -398,10 +551,26 @@ def main():
         stop.record()
         torch.cuda.synchronize()
     ms = start.elapsed_time(stop)
+    rank_ms = [ms]
+    allreduce_us = None
     if world > 1:
         t = torch.tensor([ms], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        gathered = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(gathered, t)
+        rank_ms = [float(g.item()) for g in gathered]
+        ms = max(rank_ms)
+        # the collective alone: one all-reduce of one step's partials
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for _ in range(5):
+            allreduce_partials(results2[0])
+        torch.cuda.synchronize()
+        dist.barrier()
+        a.record()
+        for _ in range(50):
+            allreduce_partials(results2[0])
+        b.record()
+        torch.cuda.synchronize()
+        allreduce_us = a.elapsed_time(b) / 50 * 1e3
     step_bytes = sum(packed_bytes) * world
     value = step_bytes * args.steps / (ms / 1e3) / 1e9
     elems = 2 * n * len(fmts) * world * args.steps / (ms / 1e3)
@@ -429,8 +598,9 @@ def main():
                                    for name, s in (("ldg", 1), ("tma", 2))}
         # every decoder this format/accumulator has, each with both strategies
         table = {}
-        for dname, dec in (("direct", 1), ("full_lut", 2), ("fraction_lut", 3),
-                           ("fraction_lut_fused", 4), ("fused_sum_lut", 5)):
+        for dname, dec in DECODERS.items():
+            if dname == "auto":
+                continue
             for sname, s in (("ldg", 1), ("tma", 2)):
                 try:
                     table[f"{dname}/{sname}"] = packed_bytes[k] / (time_kernel(k, s, dec) / 1e3) / 1e9
@@ -474,6 +644,7 @@ def main():
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+        dist.all_reduce(sync)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(args.e2e_steps):
@@ -489,13 +660,13 @@ def main():
 
     # CPU baseline + normalised error (rank 0 at N=1): the reference's CPU path
     # over the full workload on all host cores.
-    cpu_baseline, errors = None, {}
+    cpu_baseline, errors, refs = None, {}, {}
     gpu_results = host_out.numpy().copy()
+    threads = host_threads()
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
-        threads = host_threads()
         tot_bytes, tot_s, kinds = 0.0, 0.0, set()
         sample_rows = 16 if gemv else 1
-        for k, (name, _) in enumerate(fmts):
+        for k, (name, gen_kind) in enumerate(fmts):
             x, y = inputs[k]
             xw = x.cpu().numpy().view(np.uint32)
             yw = y.cpu().numpy().view(np.uint32)
@@ -510,16 +681,19 @@ def main():
                 tot_s += time.perf_counter() - t0
                 tot_bytes += (2 * cols if not gemv else cols + cols / sample_rows) * bits / 8
                 kinds.add(kind)
-                ref = np.longdouble(d[0]) + np.longdouble(d[1])
-                sabs = np.longdouble(s[0]) + np.longdouble(s[1])
-                got = np.longdouble(gpu_results[k * rows + r])
-                worst = max(worst, float(abs(got - ref) / sabs) if sabs else 0.0)
+                if not gemv:
+                    refs[(name, layout, gen_kind, n)] = (d, s)
+                worst = max(worst, normalized_error(gpu_results[k * rows + r], d, s))
             errors[name] = worst
         what = (f"{sample_rows} rows of each of the {len(fmts)} matrices ({cols} columns)"
                 if gemv else f"the full workload ({len(fmts)} DOTs x {n} values)")
         cpu_baseline = {"value": tot_bytes / tot_s / 1e9, "unit": "GB/s", "cores": threads,
                         "kind": "reference" if kinds == {"reference"} else "port",
                         "sample": what + ", host decode + compensated long-double DOT"}
+
+    per_config, raw_sweep = None, None
+    if world == 1 and not args.no_per_config and args.n == 0:
+        per_config, raw_sweep = run_per_config(ws, stream, threads, peak, refs)
 
     clk = clocks.summary()
     line = {
@@ -548,6 +722,13 @@ def main():
         "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"],
                    "reasons": clk["reasons"]},
     }
+    if world > 1:
+        line["multi_gpu"] = {"rank_ms": rank_ms, "allreduce_us": allreduce_us,
+                             "allreduce_share_of_step": (allreduce_us / 1e3) / (ms / args.steps),
+                             "collectives_per_step": 0 if gemv else 1}
+    if per_config is not None:
+        line["per_config"] = per_config
+        line["raw_sweep"] = raw_sweep
     if rank == 0:
         print(json.dumps(line), flush=True)
     ws.close()

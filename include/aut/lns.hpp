@@ -131,6 +131,19 @@ inline std::uint32_t encode(Source value) {
   return make_raw<F>(negative, static_cast<std::int32_t>(r));
 }
 
+// A fused product adds two finite log codes, each within +-(special - 1), so
+// the sum lies in [-(2 special - 2), 2 special - 2]; biased by 2 special - 2
+// it indexes a table of 4 special - 3 <= 2^B entries (product_log_bias /
+// product_log_entries, lns_benchmark_core.hpp:108-121).
+template <typename F>
+AUT_HD AUT_INLINE constexpr std::int32_t product_log_bias() {
+  return 2 * static_cast<std::int32_t>(special_log_code<F>()) - 2;
+}
+template <typename F>
+AUT_HD AUT_INLINE constexpr std::size_t product_log_entries() {
+  return std::size_t{1} << F::total_bits;
+}
+
 template <typename F> struct product_code {
   bool negative{};
   bool zero{};
@@ -146,6 +159,27 @@ AUT_HD AUT_INLINE product_code<F> multiply_codes(std::uint32_t a,
   return {sign<F>(a) != sign<F>(b), false, false,
           static_cast<std::int64_t>(log_code<F>(a)) +
               static_cast<std::int64_t>(log_code<F>(b))};
+}
+
+// The value of a product code: +-2^(log / 2^R) in the target type (one
+// exp2 of the summed logs, so one rounding instead of two), signed zero, or
+// NaN (decode_product / multiply_fused, lns_benchmark_core.hpp:256-272).
+template <typename F, typename Target>
+AUT_HD AUT_INLINE Target decode_product(product_code<F> p) {
+  if (p.nan) return std::numeric_limits<Target>::quiet_NaN();
+  if (p.zero) return p.negative ? -Target{0} : Target{0};
+  constexpr Target scale = static_cast<Target>(std::uint32_t{1} << F::log_fraction_bits);
+  Target v;
+  if constexpr (std::is_same_v<Target, float>)
+    v = ::exp2f(static_cast<float>(p.log) / scale);
+  else
+    v = ::exp2(static_cast<double>(p.log) / scale);
+  return p.negative ? -v : v;
+}
+
+template <typename F, typename Target>
+AUT_HD AUT_INLINE Target multiply_fused(std::uint32_t a, std::uint32_t b) {
+  return decode_product<F, Target>(multiply_codes<F>(a, b));
 }
 
 } // namespace aut::lns

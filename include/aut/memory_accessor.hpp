@@ -2,9 +2,12 @@
 //
 // Drop-in for the reference's include/memory_accessor.hpp:25-48: a
 // non-owning, pointer-sized view over a contiguous StorageType array whose
-// operator[] returns the element converted to ArithmeticType.  On the GPU the
-// decode-fused DOT reads such arrays through 128-bit loads; this accessor is
-// the scalar form of the same contract for user code.
+// operator[] returns the element converted to ArithmeticType.  This class
+// reproduces the reference's interface verbatim (its typedefs, constructor,
+// operator[] and data(), with the same static checks), because code written
+// against that interface must compile unchanged; it holds no algorithm.  On
+// the GPU the decode-fused DOT reads such arrays through 128-bit loads; this
+// accessor is the scalar form of the same contract for user code.
 #ifndef AUT_MEMORY_ACCESSOR_HPP_
 #define AUT_MEMORY_ACCESSOR_HPP_
 

@@ -33,7 +33,8 @@ enum {
   AUT_ERR_UNSUPPORTED = 2,      /* no kernel for format/layout/accum   */
   AUT_ERR_CUDA = 3,             /* a CUDA runtime call failed          */
   AUT_ERR_TOO_LARGE = 4,        /* size beyond a documented maximum    */
-  AUT_ERR_NO_DEVICE = 5         /* no usable CUDA device / wrong arch  */
+  AUT_ERR_NO_DEVICE = 5,        /* no usable CUDA device / wrong arch  */
+  AUT_ERR_COMM = 6              /* NCCL missing, or a collective failed */
 };
 
 /* Format families (runtime descriptor of a storage format). */
@@ -96,8 +97,13 @@ enum {
   AUT_DECODER_FRACTION_LUT = 3, /* fraction table + exponent add (lns16_r11)   */
   AUT_DECODER_FRACTION_LUT_FUSED = 4, /* logs added, one fraction lookup per
                                          pair: multiply_kind::fused (lns16_r11) */
-  AUT_DECODER_FUSED_SUM_LUT = 5 /* logs added, one lookup per pair in a table of
+  AUT_DECODER_FUSED_SUM_LUT = 5, /* logs added, one lookup per pair in a table of
                                    every product: fused_sum_lut_shared (lns8_r3) */
+  AUT_DECODER_EX2_APPROX = 6    /* logs added, one hardware ex2.approx.f32 per
+                                   pair (ex2_approx with the fused multiply,
+                                   lns_decoder_strategies.cuh:215-224; lns8_r3,
+                                   lns16_r11).  APPROXIMATE: relative error up to
+                                   2^-21 per product; never chosen by AUTO */
 };
 
 /* Sticky device status bits reported by aut_workspace_status(). */
@@ -159,6 +165,17 @@ aut_status aut_workspace_info(const aut_workspace *ws, int32_t *sm_count,
  * sticky AUT_STATUS_* bits the kernels of this workspace raised. */
 aut_status aut_workspace_status(aut_workspace *ws, uint32_t *status,
                                 int32_t clear);
+/* Failure-detection test hook (no counterpart in the reference, which has no
+ * bounded waits).  Until called again, the bulk-copy (TMA) DOT kernels
+ * launched through `ws` arm the ring stage of tile `stall_tile` of every
+ * pair without issuing its copies, and bound every barrier wait by
+ * `wait_cycles` SM clock cycles (0: the default, ~2 s).  The wait for that
+ * stage therefore runs out: the block lets its other copies land, sets
+ * AUT_STATUS_WAIT_TIMEOUT and the DOT's result is NaN.  No copy is left in
+ * flight, nothing waits without a bound, and the context stays usable.
+ * stall_tile = UINT64_MAX switches the hook off.  Not for production use. */
+aut_status aut_workspace_inject_stall(aut_workspace *ws, uint64_t stall_tile,
+                                      uint64_t wait_cycles);
 
 /* ---- the decode-fused DOT ---------------------------------------------- */
 /* result[0] = sum_i decode(x_i) * decode(y_i), written to device memory.
@@ -223,12 +240,50 @@ aut_status aut_gemv(aut_workspace *ws, int32_t format, int32_t layout,
  * at most 64 DOTs per call (batch > 64 -> AUT_ERR_TOO_LARGE); table-decoded
  * formats (LNS) -> AUT_ERR_UNSUPPORTED.  All calls share that array, so
  * calls that overlap on one GPU race; serialise them.  The first call on a
- * device looks up the array's address; make it before any stream capture.
+ * device looks up the array's address; make it before any stream capture
+ * (a failed lookup is not kept: the next call tries again; after
+ * cudaDeviceReset the kept address is stale, so do not reset a device this
+ * entry point has used).  There is no status query: a DOT whose bounded
+ * bulk-copy wait gave up reports it only as NaN in its results[b].  A call
+ * refused for its arguments or format enqueues nothing.
  * Arguments as in aut_dot_batched, on the calling thread's current device. */
 aut_status aut_dot_noalloc(int32_t format, int32_t layout, int32_t accum,
                            const void *x, const void *y, uint64_t n,
                            uint32_t batch, uint64_t batch_stride_bytes,
                            double *results, void *stream);
+
+/* ---- multi-GPU: contiguous shards and one NCCL all-reduce --------------- */
+/* The reference runs one GPU and has no collective; a DOT over a vector too
+ * long for one GPU, or spread over the GPUs of a node, is the sum of the
+ * ranks' shard DOTs.  One rank per GPU; every rank calls the same
+ * collective entry points in the same order.  NCCL (libnccl.so.2) is loaded
+ * at the first call below; without it they return AUT_ERR_COMM. */
+typedef struct aut_comm aut_comm;
+#define AUT_COMM_ID_BYTES 128
+/* A fresh communicator id (ncclGetUniqueId) into id[AUT_COMM_ID_BYTES]; one
+ * rank makes it and hands it to the others (any host channel). */
+aut_status aut_comm_unique_id(void *id);
+/* Joins the communicator `id` as `rank` of `nranks` on `device` (blocks
+ * until every rank has joined). */
+aut_status aut_comm_create(const void *id, int32_t nranks, int32_t rank,
+                           int32_t device, aut_comm **out);
+/* Uses a caller's ncclComm_t (same NCCL library as this process loads) on
+ * `device`; aut_comm_destroy then frees only the wrapper. */
+aut_status aut_comm_wrap(void *nccl_comm, int32_t device, aut_comm **out);
+aut_status aut_comm_destroy(aut_comm *comm);
+/* In-place sum over the ranks of `count` FP64 values, ordered on `stream`. */
+aut_status aut_comm_allreduce(aut_comm *comm, double *values, uint64_t count,
+                              void *stream);
+/* result[0] = the DOT of the global vectors: aut_dot of this rank's shard
+ * (x, y hold its n_local values; for dense streams a shard that starts on a
+ * whole 16-byte packet, 128 / gcd(bits, 128) values, is a byte offset into
+ * the global stream) followed by one ncclAllReduce of the FP64 partial on
+ * the same stream.  Replaces nothing in the reference (single GPU only);
+ * its per-GPU part is aut_dot. */
+aut_status aut_dot_sharded(aut_comm *comm, aut_workspace *ws, int32_t format,
+                           int32_t layout, int32_t accum, const void *x,
+                           const void *y, uint64_t n_local, double *result,
+                           void *stream);
 
 /* ---- device codecs ------------------------------------------------------ */
 /* out[i] = decode(codes[i]) as float or double, bit-identical to the

@@ -21,6 +21,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "_build", "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libautref.so")
+REFGPU_SO = os.path.join(HERE, "_ref", "librefgpu.so")
 REF_TREE = os.environ.get("AUT_REFERENCE_TREE", "/root/reference")
 
 FAMILY_BINARY, FAMILY_PREFIX, FAMILY_LNS, FAMILY_RAW_FP32, FAMILY_RAW_FP64 = range(5)
@@ -257,6 +258,37 @@ class Reference:
         self.lib.autref_dot_raw(1 if x.dtype == np.float64 else 0,
                                 x.ctypes.data, y.ctypes.data, x.size, threads, d, s)
         return _ld_pair(d), _ld_pair(s)
+
+
+class ReferenceGpu:
+    """The reference's own GPU DOT kernels (oracle/_ref/librefgpu.so, built
+    from its headers for sm_100a): run on device buffers the caller owns."""
+
+    def __init__(self, path: str = REFGPU_SO):
+        lib = C.CDLL(path)
+        self.lib = lib
+        lib.refgpu_variant_count.restype = C.c_int
+        lib.refgpu_variant_name.restype = C.c_char_p
+        lib.refgpu_variant_name.argtypes = [C.c_int]
+        lib.refgpu_run.restype = C.c_int
+        lib.refgpu_run.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_uint64, C.c_int,
+                                   C.POINTER(C.c_double), C.POINTER(C.c_double)]
+        self.variants = [lib.refgpu_variant_name(i).decode()
+                         for i in range(lib.refgpu_variant_count())]
+
+    def run(self, name: str, x_ptr: int, y_ptr: int, n: int, reps: int = 10):
+        """(result, ms per DOT) of variant `name`."""
+        res, ms = C.c_double(), C.c_double()
+        rc = self.lib.refgpu_run(self.variants.index(name), x_ptr, y_ptr, n, reps,
+                                 C.byref(res), C.byref(ms))
+        if rc != 0:
+            raise RuntimeError(f"reference kernel {name} failed ({rc})")
+        return res.value, ms.value
+
+
+def reference_gpu():
+    """The reference's GPU kernels, or None when librefgpu.so was not built."""
+    return ReferenceGpu() if os.path.exists(REFGPU_SO) else None
 
 
 def oracle() -> Oracle:

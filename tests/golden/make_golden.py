@@ -15,6 +15,13 @@ Fixtures written (all small, all produced by the reference's own code):
   dot_vectors.json    -- reference CPU DOTs (host decode + compensated long
                          double sum) of the synthetic workloads at small N,
                          with an FNV-1a fingerprint of each packed stream.
+  accessor_dot_accuracy.csv
+                      -- the normalised errors the reference's own GPU
+                         kernels reached on the dot_v1 cases (FP32 storage,
+                         FP32 / FP64 accumulation; raw and accessor DOT),
+                         copied from its published run
+                         results/003_accessor_dot/run_20260723T150439Z/
+                         accuracy_comparison.csv (H200, sm_90).
 """
 from __future__ import annotations
 
@@ -122,6 +129,20 @@ def main() -> None:
                               "sum_abs_hi": s[0], "sum_abs_lo": s[1]})
     with open(os.path.join(HERE, "dot_vectors.json"), "w") as f:
         json.dump(dots, f, indent=1)
+
+    # 4. the reference GPU kernels' published normalised errors on dot_v1.
+    import csv as _csv
+    src = os.path.join(pyoracle.REF_TREE, "results", "003_accessor_dot",
+                       "run_20260723T150439Z", "accuracy_comparison.csv")
+    keep = ["dataset", "n", "dot_condition_number", "raw_f32_normalized_error",
+            "accessor_f32_f32_normalized_error", "raw_f64_normalized_error",
+            "accessor_f64_f32_normalized_error"]
+    with open(src) as f:
+        rows = list(_csv.DictReader(f))
+    with open(os.path.join(HERE, "accessor_dot_accuracy.csv"), "w") as f:
+        f.write(",".join(keep) + "\n")
+        for r in rows:
+            f.write(",".join(r[k] for k in keep) + "\n")
     print("golden fixtures written to", HERE)
 
 

@@ -82,7 +82,8 @@ def test_decoders_without_a_kernel_are_refused(ws):
     refused = [("lns16_r11", 1, 2), ("lns16_r11", 0, 1), ("lns8_r3", 0, 3),
                ("lns8_r3", 0, 4), ("lns8_r3", 0, 1), ("e8m15", 0, 2), ("bf16_e8m7", 1, 2),
                ("fp32", 0, 2), ("e8m0", 0, 3), ("fp32", 0, 3),
-               ("e8m15", 1, 4), ("lns16_r11", 0, 5), ("e8m0", 0, 5), ("fp64", 1, 5)]
+               ("e8m15", 1, 4), ("lns16_r11", 0, 5), ("e8m0", 0, 5), ("fp64", 1, 5),
+               ("e8m0", 0, 6), ("e2m3", 1, 6), ("fp32", 1, 6)]
     for name, accum, decoder in refused:
         with pytest.raises(_lib.AutError) as info:
             ws.dot(_lib.format_id(name), 0, accum, x.data_ptr(), x.data_ptr(), 64,
@@ -90,7 +91,7 @@ def test_decoders_without_a_kernel_are_refused(ws):
         assert info.value.status == _lib.AUT_ERR_UNSUPPORTED, (name, accum, decoder)
     with pytest.raises(_lib.AutError) as info:
         ws.dot(_lib.format_id("e8m0"), 0, 0, x.data_ptr(), x.data_ptr(), 64,
-               res.data_ptr(), decoder=6)
+               res.data_ptr(), decoder=7)
     assert info.value.status == _lib.AUT_ERR_INVALID_ARGUMENT
 
 

@@ -1,0 +1,103 @@
+"""libautdot beside the reference's own GPU kernels on the same B200.
+
+The reference's dot_thread_kernel + finalize_dot_kernel (bit formats,
+bitwidth_benchmark_kernels.cuh:403-457), raw_dot_kernel (:681-703) and its
+LNS kernel (lns_benchmark_kernels.cuh:80-131), compiled from its headers for
+sm_100a (oracle/_ref/librefgpu.so) and launched the way its benchmarks
+launch them, run on the very device buffers libautdot reads, at the
+benchmark's sizes.  Both DOTs are compared with the reference's compensated
+long-double CPU DOT of the same codes.  The north star asks that the
+normalised error be no worse than the reference's own kernel for the same
+format and accumulator: asserted for every exact decoder of the
+reference; the approximate ex2 variants are printed only.  The GB/s of both
+(CUDA events, inputs larger than L2) are printed.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from gpu_util import SEED, normalized_error
+
+pytestmark = pytest.mark.gpu
+
+THREADS = max(1, len(os.sched_getaffinity(0)))
+# (format, generator kind, n) at the benchmark configurations' sizes
+CASES = [("fp32", 1, 1 << 27), ("fp64", 0, 1 << 27), ("e2m3", 2, 1 << 27),
+         ("e8m0", 0, 1 << 27), ("e8m1", 0, 1 << 27), ("e8m3", 0, 1 << 27),
+         ("e8m5", 0, 1 << 27), ("bf16_e8m7", 0, 1 << 27), ("e8m15", 0, 1 << 27),
+         ("lns8_r3", 3, 1 << 28), ("lns16_r11", 3, 1 << 28)]
+
+
+@pytest.fixture(scope="module")
+def refgpu():
+    import pyoracle
+    r = pyoracle.reference_gpu()
+    if r is None:
+        pytest.skip("oracle/_ref/librefgpu.so not built (needs the reference tree)")
+    return r
+
+
+def _cpu_dot(name, bits, stride, xw, yw, n):
+    import pyoracle
+    ref = pyoracle.reference()
+    if ref is not None and name in ref.formats:
+        d, s = ref.dot_dense(name, stride, xw, yw, n, THREADS)
+    elif ref is not None:
+        dt = np.float32 if name == "fp32" else np.float64
+        d, s = ref.dot_raw(xw.view(dt)[:n], yw.view(dt)[:n], THREADS)
+    else:
+        from accessor_universal_test_b200 import _lib
+        desc = _lib.format_info(_lib.format_id(name))
+        d, s = pyoracle.oracle().dot_dense(desc, stride, xw, yw, n, THREADS)
+    return (np.longdouble(d[0]) + np.longdouble(d[1]),
+            np.longdouble(s[0]) + np.longdouble(s[1]))
+
+
+@pytest.mark.parametrize("name,kind,n", CASES)
+def test_error_no_worse_than_the_reference_kernel(ws, refgpu, name, kind, n):
+    import torch
+    from accessor_universal_test_b200 import _lib, vectors
+    fid = _lib.format_id(name)
+    ws.prepare(fid)
+    bits = _lib.format_info(fid)[1]
+    packed = 2 * n * bits / 8
+    layouts = [0] if bits in (32, 64) or name.startswith("lns") else [0, 1]
+    rows = []
+    for layout in layouts:
+        lname = "raw" if bits in (32, 64) else ("dense" if layout == 0 else "padded")
+        x = vectors.encoded(ws, fid, layout, kind, SEED, 0, n)
+        y = vectors.encoded(ws, fid, layout, kind, SEED, 1, n)
+        torch.cuda.synchronize()
+        stride = 64 if name == "fp64" else (bits if layout == 0 else
+                                            (8 if bits <= 8 else 16 if bits <= 16 else 32))
+        ref_dot, ref_abs = _cpu_dot(name, bits, stride, x.cpu().numpy().view(np.uint32),
+                                    y.cpu().numpy().view(np.uint32), n)
+        res = torch.zeros(1, dtype=torch.float64, device="cuda")
+        for variant in [v for v in refgpu.variants
+                        if v.split("/")[0] == name and v.split("/")[2] == lname]:
+            acc = 0 if variant.split("/")[1] == "fp32" else 1
+            theirs, t_ms = refgpu.run(variant, x.data_ptr(), y.data_ptr(), n, reps=10)
+            e_theirs = float(normalized_error(theirs, ref_dot, ref_abs))
+
+            def ours_launch():
+                ws.dot(fid, layout, acc, x.data_ptr(), y.data_ptr(), n, res.data_ptr())
+            ours_launch()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(10):
+                ours_launch()
+            b.record()
+            torch.cuda.synchronize()
+            o_ms = a.elapsed_time(b) / 10
+            ours = float(res.item())
+            e_ours = float(normalized_error(ours, ref_dot, ref_abs))
+            rows.append((variant, packed / t_ms / 1e6, e_theirs, packed / o_ms / 1e6, e_ours))
+            if "ex2_approx" not in variant:
+                assert e_ours <= e_theirs * (1 + 1e-9) + 1e-300, (variant, e_ours, e_theirs)
+        del x, y
+        torch.cuda.empty_cache()
+    for v, tg, te, og, oe in rows:
+        print(f"REFKERNEL {v:45s} reference {tg:8.1f} GB/s err {te:.3e} | "
+              f"libautdot {og:8.1f} GB/s err {oe:.3e} | x{og / tg:.2f}")

@@ -153,3 +153,20 @@ def test_errors_are_reported_not_raised(autlib):
     res = C.c_double()
     assert autlib.aut_dot(None, 3, 0, 0, None, None, 0, C.byref(res), None) == \
         _lib.AUT_ERR_INVALID_ARGUMENT
+
+
+def test_collective_entry_points_check_their_arguments(autlib):
+    """aut_comm_* / aut_dot_sharded refuse bad arguments before touching NCCL
+    or a GPU."""
+    from accessor_universal_test_b200 import _lib
+    res = C.c_double()
+    assert autlib.aut_dot_sharded(None, None, 3, 0, 0, None, None, 0, C.byref(res), None) == \
+        _lib.AUT_ERR_INVALID_ARGUMENT
+    assert b"communicator" in autlib.aut_last_error()
+    h = C.c_void_p()
+    ident = C.create_string_buffer(_lib.COMM_ID_BYTES)
+    assert autlib.aut_comm_create(ident, 2, 2, 0, C.byref(h)) == _lib.AUT_ERR_INVALID_ARGUMENT
+    assert autlib.aut_comm_create(None, 2, 0, 0, C.byref(h)) == _lib.AUT_ERR_INVALID_ARGUMENT
+    assert autlib.aut_comm_unique_id(None) == _lib.AUT_ERR_INVALID_ARGUMENT
+    assert autlib.aut_comm_allreduce(None, None, 1, None) == _lib.AUT_ERR_INVALID_ARGUMENT
+    assert autlib.aut_comm_destroy(None) == _lib.AUT_OK

@@ -3,10 +3,11 @@ memory (their GPU memory belongs to another framework's pool, or a
 cudaMalloc would stall a latency-critical path).  Its reduction scratch is a
 fixed device array inside the library instead of a workspace.
 
-Checked through the C ABI against the workspace entry point (aut_dot), twice
-in a row so the second call runs on the scratch the first one left behind.
-This file sorts last so that a run stopping at its first failure has run
-every other test already.
+Checked through the C ABI against the workspace entry point (aut_dot) and
+the oracle's compensated long-double DOT, twice in a row so the second call
+runs on the scratch the first one left behind; both layouts, pointers off
+the 16-byte grid (the per-value path) and n = 0.  This file sorts last so
+that a run stopping at its first failure has run every other test already.
 """
 import ctypes as C
 
@@ -31,19 +32,63 @@ def test_noalloc_dot_matches_workspace_dot_twice_in_a_row(ws, orc, name):
     from accessor_universal_test_b200 import _lib
     fid = _lib.format_id(name)
     n = (1 << 21) + 77
-    x, y = device_pair(ws, name, _lib.DENSE, n)
-    _, ref_abs = oracle_dot(orc, name, n)
-    accums = [a for a in (0, 1) if _lib.load().aut_dot_supported(fid, _lib.DENSE, a)]
-    for accum in accums:
-        want = gpu_dot(ws, name, _lib.DENSE, accum, x, y, n)
+    for layout in (_lib.DENSE, _lib.PADDED):
+        x, y = device_pair(ws, name, layout, n)
+        ref_dot, ref_abs = oracle_dot(orc, name, n)
+        accums = [a for a in (0, 1) if _lib.load().aut_dot_supported(fid, layout, a)]
+        for accum in accums:
+            want = gpu_dot(ws, name, layout, accum, x, y, n)
+            for call in range(2):
+                res = torch.full((1,), float("nan"), dtype=torch.float64, device="cuda")
+                st = _noalloc(fid, layout, accum, x.data_ptr(), y.data_ptr(), n, 1, 0,
+                              res.data_ptr())
+                assert st == _lib.AUT_OK, _lib.load().aut_last_error()
+                torch.cuda.synchronize()
+                got = float(res.item())
+                assert abs(got - want) <= TOL[accum] * float(ref_abs), (
+                    name, layout, accum, call, got, want)
+                err = abs(np.longdouble(got) - ref_dot) / ref_abs
+                assert err <= TOL[accum], (name, layout, accum, call, got, float(ref_dot))
+
+
+@pytest.mark.parametrize("name,layout", [("e8m1", 0), ("e2m3", 1), ("fp32", 0)])
+def test_noalloc_off_grid_pointers_take_the_per_value_path(ws, orc, name, layout):
+    """The same streams copied to start 4 bytes past a 16-byte boundary:
+    both entry points read them value by value."""
+    import torch
+    from accessor_universal_test_b200 import _lib
+    fid = _lib.format_id(name)
+    n = 100_003
+    x, y = device_pair(ws, name, layout, n)
+    xs = torch.zeros(x.numel() + 16, dtype=torch.uint8, device="cuda")
+    ys = torch.zeros(y.numel() + 16, dtype=torch.uint8, device="cuda")
+    xs[4:4 + x.numel()] = x
+    ys[4:4 + y.numel()] = y
+    ref_dot, ref_abs = oracle_dot(orc, name, n)
+    for accum in (0, 1):
+        want = gpu_dot(ws, name, layout, accum, xs, ys, n, x_off=4, y_off=4)
         for call in range(2):
             res = torch.full((1,), float("nan"), dtype=torch.float64, device="cuda")
-            st = _noalloc(fid, _lib.DENSE, accum, x.data_ptr(), y.data_ptr(), n, 1, 0,
-                          res.data_ptr())
-            assert st == _lib.AUT_OK, _lib.load().aut_last_error()
+            assert _noalloc(fid, layout, accum, xs.data_ptr() + 4, ys.data_ptr() + 4, n, 1, 0,
+                            res.data_ptr()) == _lib.AUT_OK, _lib.load().aut_last_error()
             torch.cuda.synchronize()
             got = float(res.item())
             assert abs(got - want) <= TOL[accum] * float(ref_abs), (name, accum, call, got, want)
+            err = abs(np.longdouble(got) - ref_dot) / ref_abs
+            assert err <= TOL[accum], (name, accum, call, got, float(ref_dot))
+
+
+def test_noalloc_empty_vectors_give_zero(ws):
+    import torch
+    from accessor_universal_test_b200 import _lib
+    fid = _lib.format_id("e8m0")
+    buf = torch.zeros(64, dtype=torch.uint8, device="cuda")
+    for call in range(2):
+        res = torch.full((2,), float("nan"), dtype=torch.float64, device="cuda")
+        assert _noalloc(fid, _lib.DENSE, 0, buf.data_ptr(), buf.data_ptr(), 0, 2, 16,
+                        res.data_ptr()) == _lib.AUT_OK, _lib.load().aut_last_error()
+        torch.cuda.synchronize()
+        assert res.cpu().tolist() == [0.0, 0.0], call
 
 
 def test_noalloc_batch_matches_single_dots(ws, orc):
