@@ -27,7 +27,8 @@ ACC_FP32, ACC_FP64 = 0, 1
 TARGET_FP32, TARGET_FP64 = 0, 1
 STRATEGY_AUTO, STRATEGY_LDG, STRATEGY_TMA, STRATEGY_SCALAR = 0, 1, 2, 3
 (DECODER_AUTO, DECODER_DIRECT, DECODER_FULL_LUT, DECODER_FRACTION_LUT,
- DECODER_FRACTION_LUT_FUSED, DECODER_FUSED_SUM_LUT, DECODER_EX2_APPROX) = range(7)
+ DECODER_FRACTION_LUT_FUSED, DECODER_FUSED_SUM_LUT, DECODER_EX2_APPROX,
+ DECODER_PREFIX_LUT, DECODER_SUBNORMAL_LUT) = range(9)
 STATUS_WAIT_TIMEOUT = 1
 GEN_SIGNED_UNIT_F64, GEN_SIGNED_UNIT_F32, GEN_NORMAL, GEN_LNS_CANCEL, GEN_POSITIVE_UNIT_F64 = range(5)
 
@@ -67,6 +68,7 @@ SIGNATURES = {
     "aut_decode": (_i32, [_vp, _i32, _i32, _i32, _vp, _u64, _vp, _vp]),
     "aut_encode": (_i32, [_vp, _i32, _i32, _vp, _u64, _vp, _vp]),
     "aut_generate": (_i32, [_i32, _u64, _i32, _u64, _u64, _vp, _vp]),
+    "aut_generate_dot_v1": (_i32, [_i32, _u64, _i32, _i32, _u64, _u64, _u64, _vp, _vp]),
     "aut_encode_host": (_i32, [_i32, _vp, _u64, _vp]),
     "aut_decode_host": (_i32, [_i32, _vp, _u64, _vp]),
     "aut_pack_host": (_i32, [_i32, _i32, _vp, _u64, _vp]),
@@ -179,6 +181,14 @@ class Workspace:
 
     def encode(self, fmt, layout, values_ptr, n, codes_ptr, stream=0) -> None:
         check(load().aut_encode(self.handle, fmt, layout, values_ptr, n, codes_ptr, stream))
+
+
+def generate_dot_v1(family: int, seed: int, parameter: int, vector_id: int, count: int,
+                    out_ptr, first: int = 0, n: int | None = None, stream=0) -> None:
+    """Values [first, first + n) of a dot_v1 case vector (FP32, on the device)."""
+    n = count - first if n is None else n
+    check(load().aut_generate_dot_v1(family, seed, parameter, vector_id, count, first, n,
+                                     out_ptr, stream))
 
 
 def comm_unique_id() -> bytes:

@@ -11,6 +11,7 @@
 #include "internal.hpp"
 
 #include "aut/detail/codec_core.hpp"
+#include "aut/dot_dataset.hpp"
 
 #include <cuda_runtime.h>
 
@@ -225,6 +226,15 @@ __global__ void generate_kernel(int kind, uint64_t seed, int vector_id,
     out[i] = synthetic(kind, seed, vector_id, first + i);
 }
 
+// Values [first, first + n) of vector `vector_id` of a dot_v1 case of `count`
+// values (dot_dataset.hpp: the reference's generators, bit for bit).
+__global__ void generate_dot_v1_kernel(aut::dataset::parameters spec, int vector_id,
+                                       uint64_t count, uint64_t first, uint64_t n, float *out) {
+  for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x;
+       i < n; i += static_cast<uint64_t>(gridDim.x) * blockDim.x)
+    out[i] = aut::dataset::value(spec, vector_id, first + i, count);
+}
+
 // ---- the generic DOT: any registered format, one value per thread ---------------
 // The runtime switch over the registry (the reference compiles one binary per
 // width, src/bitwidth_strategy_bench.cu:955-1211): codes are read by absolute
@@ -386,6 +396,20 @@ aut_status launch_generate(int32_t kind, uint64_t seed, int32_t vector_id,
   if (n == 0) return AUT_OK;
   aut::dev::generate_kernel<<<grid_for(n), 256, 0, stream>>>(kind, seed, vector_id,
                                                              first, n, out);
+  AUT_CUDA_TRY(cudaGetLastError());
+  return AUT_OK;
+}
+
+aut_status launch_generate_dot_v1(int32_t family, uint64_t seed, int32_t parameter,
+                                  int32_t vector_id, uint64_t count, uint64_t first,
+                                  uint64_t n, float *out, cudaStream_t stream) {
+  if (n == 0) return AUT_OK;
+  aut::dataset::parameters spec;
+  spec.kind = static_cast<aut::dataset::family>(family);
+  spec.seed = seed;
+  spec.parameter = parameter;
+  aut::dev::generate_dot_v1_kernel<<<grid_for(n), 256, 0, stream>>>(spec, vector_id, count,
+                                                                    first, n, out);
   AUT_CUDA_TRY(cudaGetLastError());
   return AUT_OK;
 }

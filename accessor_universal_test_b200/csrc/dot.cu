@@ -285,15 +285,14 @@ template <int S> struct e2m3_codec {
   }
 };
 
-// Copies of a small decode table in shared memory, one per lane group, so a
+// Copies of a small decode table in shared memory, one per lane, so a
 // warp's lookups never share a bank: entry e of copy c at element
-// e * kCopies + c.  A warp's 4-byte loads are served together, so 4-byte
-// entries need a copy per lane; 8-byte loads are served a half warp at a
-// time (16 lanes x 8 bytes span the 32 banks once), so 16 copies of 8-byte
-// entries are conflict-free and take half the space (256 FP64 entries: 32
-// KiB instead of 64, which lets twice as many blocks share an SM).
+// e * kCopies + c.  (8-byte entries would be conflict-free with 16 copies,
+// a half warp per wavefront, but the extra blocks that the halved table
+// lets onto an SM then saturate the shared-memory pipe: lns8_r3 with the
+// FP64 accumulator, 3650 -> 3355 GB/s; 32 copies are kept.)
 template <typename T> struct lane_table {
-  static constexpr int kCopies = sizeof(T) == 8 ? 16 : 32;
+  static constexpr int kCopies = 32;
   static constexpr uint32_t kEntryBytes = kCopies * static_cast<uint32_t>(sizeof(T));
   static constexpr int bytes(int entries) { return entries * static_cast<int>(kEntryBytes); }
   __device__ __forceinline__ static uint32_t lane_offset() {
@@ -932,6 +931,84 @@ template <int S, int W, typename T> struct wide_lut_codec {
                                                 Acc &acc, const unsigned char *smem) {
     acc.mac_d(0, static_cast<double>(value(load_code<S, W>(xb, i), smem)),
               static_cast<double>(value(load_code<S, W>(yb, j), smem)));
+  }
+};
+
+// The reference's partial-table decoders of the E8 codes with 1 to 5
+// mantissa bits (decode_with_table with prefix_lut_shared /
+// subnormal_lut_shared, bitwidth_benchmark_kernels.cuh:229-259; they exist
+// for formats of >= 9 bits with >= 2 exponent and >= 1 mantissa bits).
+//   PREFIX:    a 512-entry table indexed by sign and exponent holds the
+//              target's sign and exponent field (FP32 bits / FP64 high
+//              word); the mantissa is ORed below it.  Zero/subnormal and
+//              inf/NaN exponents take the direct bit move instead.
+//   SUBNORMAL: a 2^M-entry table holds the subnormal values (exponent 0);
+//              every other code takes the direct bit move.
+// Both select between table and direct decode without branching.  They are
+// exact and slower than the bit moves alone (one shared load and a select
+// per code), kept for the decoder axis; AUTO never picks them.
+template <int S, int W, typename T, bool kPrefix> struct part_lut_codec {
+  static constexpr int kS = S;
+  static constexpr int kW = W;
+  static constexpr int kM = W - 9;
+  static_assert(kM >= 1 && kM <= 5, "E8 codes with 1 to 5 mantissa bits");
+  static constexpr int kEntries = kPrefix ? 512 : (1 << kM);
+  static constexpr int kTableBytes = kEntries * 4 < 16 ? 16 : kEntries * 4;
+  static constexpr int kU = packet_shape<S>::Q == 1 ? 4 : 1;
+  static constexpr bool kExactLanes = false;
+  // mantissa position in the target word (FP32 bits / FP64 high word)
+  static constexpr int kShift = (sizeof(T) == 4 ? 23 : 20) - kM;
+
+  __device__ static void prepare(const dot_params &p, unsigned char *smem) {
+    const uint32_t *g = static_cast<const uint32_t *>(p.table);
+    uint32_t *t = reinterpret_cast<uint32_t *>(smem);
+    for (int e = threadIdx.x; e < kEntries; e += kThreads) t[e] = g[e];
+  }
+
+  __device__ __forceinline__ static T decode(uint32_t c, const uint32_t *tab) {
+    const uint32_t e = (c >> kM) & 0xffu;
+    const uint32_t f = c & ((1u << kM) - 1u);
+    const uint32_t direct = c << (32 - W);  // FP32 bits, exact for every code
+    uint32_t word;
+    bool use_table;
+    if constexpr (kPrefix) {
+      word = tab[c >> kM] | (f << kShift);
+      use_table = e - 1u < 254u;  // a normal exponent
+    } else {
+      word = tab[f] | ((c >> (W - 1)) << 31);
+      use_table = e == 0u;
+    }
+    if constexpr (sizeof(T) == 4) {
+      return __uint_as_float(use_table ? word : direct);
+    } else {
+      const double d = static_cast<double>(__uint_as_float(direct));
+      const double w = __hiloint2double(static_cast<int>(word), 0);
+      return use_table ? w : d;
+    }
+  }
+
+  template <int NV, class Acc>
+  __device__ __forceinline__ static void values(const uint32_t *xw, const uint32_t *yw,
+                                                Acc &acc, float *, const unsigned char *smem) {
+    const uint32_t *tab = reinterpret_cast<const uint32_t *>(smem);
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const T a = decode(field_low<S, W>(xw, v), tab);
+      const T b = decode(field_low<S, W>(yw, v), tab);
+      if constexpr (sizeof(T) == 4)
+        acc.mac(v, a, b);
+      else
+        acc.mac_d(v, a, b);
+    }
+  }
+
+  template <class Acc>
+  __device__ __forceinline__ static void scalar(const unsigned char *xb, uint64_t i,
+                                                const unsigned char *yb, uint64_t j, Acc &acc,
+                                                const unsigned char *smem) {
+    const uint32_t *tab = reinterpret_cast<const uint32_t *>(smem);
+    acc.mac_d(0, static_cast<double>(decode(load_code<S, W>(xb, i), tab)),
+              static_cast<double>(decode(load_code<S, W>(yb, j), tab)));
   }
 };
 
@@ -1862,6 +1939,16 @@ kernel_entry pick(int strategy, int accum, int table_kind) {
              : make_entry<Codec, aut::dev::acc_f64>(strategy, table_kind);
 }
 
+// table kinds 8-11: prefix (FP32 bits / FP64 high word), subnormal (same)
+template <int S, int W, bool kPrefix>
+kernel_entry part_pick(int strategy, int accum) {
+  using namespace aut::dev;
+  const int kind = (kPrefix ? 8 : 10) + (accum == AUT_ACCUM_FP32 ? 0 : 1);
+  return accum == AUT_ACCUM_FP32
+             ? make_entry<part_lut_codec<S, W, float, kPrefix>, acc_f32>(strategy, kind)
+             : make_entry<part_lut_codec<S, W, double, kPrefix>, acc_f64>(strategy, kind);
+}
+
 template <int S, int W>
 kernel_entry wide_pick(int strategy, int accum) {
   using namespace aut::dev;
@@ -1926,6 +2013,22 @@ kernel_entry lookup(int32_t format, int32_t layout, int32_t accum, int strategy,
     default: return {};
     }
   }
+  if (decoder == AUT_DECODER_PREFIX_LUT || decoder == AUT_DECODER_SUBNORMAL_LUT) {
+    // the partial-table decoders of the E8 codes with 1 to 5 mantissa bits
+    const bool pre = decoder == AUT_DECODER_PREFIX_LUT;
+    switch (format) {
+    case AUT_FMT_E8M1:
+      return dense ? (pre ? part_pick<10, 10, true>(s, accum) : part_pick<10, 10, false>(s, accum))
+                   : (pre ? part_pick<16, 10, true>(s, accum) : part_pick<16, 10, false>(s, accum));
+    case AUT_FMT_E8M3:
+      return dense ? (pre ? part_pick<12, 12, true>(s, accum) : part_pick<12, 12, false>(s, accum))
+                   : (pre ? part_pick<16, 12, true>(s, accum) : part_pick<16, 12, false>(s, accum));
+    case AUT_FMT_E8M5:
+      return dense ? (pre ? part_pick<14, 14, true>(s, accum) : part_pick<14, 14, false>(s, accum))
+                   : (pre ? part_pick<16, 14, true>(s, accum) : part_pick<16, 14, false>(s, accum));
+    default: return {};
+    }
+  }
   if (decoder != AUT_DECODER_AUTO) {
     if (!lns && decoder != AUT_DECODER_DIRECT) return {};
     if (lns && decoder == AUT_DECODER_DIRECT) return {};
@@ -1938,10 +2041,14 @@ kernel_entry lookup(int32_t format, int32_t layout, int32_t accum, int strategy,
     // never chosen by AUTO: approximate
     if (format == AUT_FMT_LNS8_R3)
       return accum == AUT_ACCUM_FP32 ? make_entry<lns_ex2_codec<8, float>, acc_f32>(s, 0)
-                                     : make_entry<lns_ex2_codec<8, double>, acc_f64>(s, 0);
+                                     : make_entry<lns_ex2_codec<8, double>, acc_f64c>(s, 0);
     return accum == AUT_ACCUM_FP32 ? make_entry<lns_ex2_codec<16, float>, acc_f32>(s, 0)
-                                   : make_entry<lns_ex2_codec<16, double>, acc_f64>(s, 0);
+                                   : make_entry<lns_ex2_codec<16, double>, acc_f64c>(s, 0);
   }
+  // LNS with the FP64 accumulator: products of two table values round, and
+  // on data whose signs alternate the two FMA chains of acc_f64 would each
+  // collect one sign; acc_f64c keeps every product's and every addition's
+  // rounding error instead.
   if (format == AUT_FMT_LNS16_R11) {
     const bool f32 = accum == AUT_ACCUM_FP32;
     switch (decoder) {
@@ -1950,10 +2057,10 @@ kernel_entry lookup(int32_t format, int32_t layout, int32_t accum, int strategy,
       return make_entry<lns16_full_codec, acc_f32>(s, 1);
     case AUT_DECODER_FRACTION_LUT:
       return f32 ? make_entry<lns16_codec<float>, acc_f32>(s, 3)
-                 : make_entry<lns16_codec<double>, acc_f64>(s, 4);
+                 : make_entry<lns16_codec<double>, acc_f64c>(s, 4);
     default:  // AUTO, FRACTION_LUT_FUSED
       return f32 ? make_entry<lns16_fused_codec<float>, acc_f32>(s, 3)
-                 : make_entry<lns16_fused_codec<double>, acc_f64>(s, 4);
+                 : make_entry<lns16_fused_codec<double>, acc_f64c>(s, 4);
     }
   }
   switch (format) {
@@ -1976,13 +2083,18 @@ kernel_entry lookup(int32_t format, int32_t layout, int32_t accum, int strategy,
     return dense ? pick<e8_codec<14, 14>>(s, accum, 0) : pick<e8_codec<16, 14>>(s, accum, 0);
   case AUT_FMT_BF16_E8M7: return pick<e8_codec<16, 16>>(s, accum, 0);
   case AUT_FMT_E8M15:
+    // 16-bit significands: FP32 products round, so the FP32 accumulator is
+    // compensated (acc_f32c); the bulk copies keep the kernel HBM-bound
+    if (accum == AUT_ACCUM_FP32)
+      return dense ? make_entry<e8_codec<24, 24>, acc_f32c>(s, 0)
+                   : make_entry<e8_codec<32, 24>, acc_f32c>(s, 0);
     return dense ? pick<e8_codec<24, 24>>(s, accum, 0) : pick<e8_codec<32, 24>>(s, accum, 0);
   case AUT_FMT_LNS8_R3:
     if (decoder == AUT_DECODER_FUSED_SUM_LUT)
       return accum == AUT_ACCUM_FP32 ? make_entry<lns8_fused_codec<float>, acc_f32>(s, 5)
-                                     : make_entry<lns8_fused_codec<double>, acc_f64>(s, 6);
+                                     : make_entry<lns8_fused_codec<double>, acc_f64c>(s, 6);
     return accum == AUT_ACCUM_FP32 ? make_entry<lns8_codec<float>, acc_f32>(s, 1)
-                                   : make_entry<lns8_codec<double>, acc_f64>(s, 2);
+                                   : make_entry<lns8_codec<double>, acc_f64c>(s, 2);
   default: return {};
   }
 }
@@ -2126,9 +2238,17 @@ aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
                   "this host's exp2/exp2f break the split LNS decode identity that the "
                   "fraction-table kernels rely on");
     if ((e.table_kind == 7 && t->full_hi == nullptr) ||
-        ((e.table_kind == 5 || e.table_kind == 6) && t->prod_f32 == nullptr))
+        ((e.table_kind == 5 || e.table_kind == 6) && t->prod_f32 == nullptr) ||
+        (e.table_kind >= 8 && t->part == nullptr))
       return fail(AUT_ERR_UNSUPPORTED, "no decode table of this kind for this format");
-    table = e.table_kind == 1   ? static_cast<const void *>(t->full_f32)
+    const uint32_t sub_entries = t->part_sub_entries;
+    table = e.table_kind >= 8
+                ? static_cast<const void *>(
+                      t->part + (e.table_kind == 8   ? 0
+                                 : e.table_kind == 9 ? 512
+                                 : e.table_kind == 10 ? 1024
+                                                      : 1024 + sub_entries))
+            : e.table_kind == 1 ? static_cast<const void *>(t->full_f32)
             : e.table_kind == 2 ? static_cast<const void *>(t->full_f64)
             : e.table_kind == 5 ? static_cast<const void *>(t->prod_f32)
             : e.table_kind == 6 ? static_cast<const void *>(t->prod_f64)

@@ -52,6 +52,11 @@ struct code_tables {
   // bit formats of 9 to 14 bits whose FP64 values all have a zero low word:
   // the high word per code (the reference's full table for the FP64 target)
   uint32_t *full_hi = nullptr;  // 2^B entries
+  // E8 codes with 1 to 5 mantissa bits: the partial tables of the prefix and
+  // subnormal decoders, [512 prefix FP32 words | 512 prefix FP64 high words
+  // | 2^M subnormal FP32 words | 2^M subnormal FP64 high words]
+  uint32_t *part = nullptr;
+  uint32_t part_sub_entries = 0;
   // LNS only:
   float *frac_f32 = nullptr;   // 2^R entries: exp2f(f / 2^R)
   double *frac_f64 = nullptr;  // 2^R entries: exp2(f / 2^R)

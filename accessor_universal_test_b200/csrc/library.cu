@@ -267,6 +267,37 @@ aut_status build_code_tables(const format_desc &f, code_tables &t) {
       AUT_CUDA_TRY(cudaMalloc(&t.full_hi, full * sizeof(uint32_t)));
       AUT_CUDA_TRY(cudaMemcpy(t.full_hi, hi.data(), full * sizeof(uint32_t), cudaMemcpyHostToDevice));
     }
+    const int M = Bb - 1 - f.exponent_bits;
+    if (f.family == AUT_FAMILY_BINARY && f.exponent_bits == 8 && M >= 1 && M <= 5) {
+      // prefix entries: the value of (sign, exponent, mantissa 0) with its
+      // fraction bits cleared; subnormal entries: the value of (0, 0, f)
+      const uint32_t sub = 1u << M;
+      std::vector<uint32_t> part(1024 + 2 * sub);
+      for (uint32_t pfx = 0; pfx < 512; ++pfx) {
+        const double v = decode_host(f, pfx << M);
+        const float v32 = static_cast<float>(v);
+        uint32_t b32;
+        uint64_t b64;
+        std::memcpy(&b32, &v32, sizeof b32);
+        std::memcpy(&b64, &v, sizeof b64);
+        part[pfx] = b32 & 0xff800000u;
+        part[512 + pfx] = static_cast<uint32_t>(b64 >> 32) & 0xfff00000u;
+      }
+      for (uint32_t fr = 0; fr < sub; ++fr) {
+        const double v = decode_host(f, fr);
+        const float v32 = static_cast<float>(v);
+        uint32_t b32;
+        uint64_t b64;
+        std::memcpy(&b32, &v32, sizeof b32);
+        std::memcpy(&b64, &v, sizeof b64);
+        part[1024 + fr] = b32;
+        part[1024 + sub + fr] = static_cast<uint32_t>(b64 >> 32);
+      }
+      AUT_CUDA_TRY(cudaMalloc(&t.part, part.size() * sizeof(uint32_t)));
+      AUT_CUDA_TRY(cudaMemcpy(t.part, part.data(), part.size() * sizeof(uint32_t),
+                              cudaMemcpyHostToDevice));
+      t.part_sub_entries = sub;
+    }
     t.ready = 1;
     return AUT_OK;
   }
@@ -349,6 +380,7 @@ void free_code_tables(code_tables &t) {
   cudaFree(t.full_f32);
   cudaFree(t.full_f64);
   cudaFree(t.full_hi);
+  cudaFree(t.part);
   cudaFree(t.frac_f32);
   cudaFree(t.frac_f64);
   cudaFree(t.prod_f32);
@@ -411,6 +443,9 @@ aut_status launch_decode(aut_workspace *ws, const format_desc &f, int32_t format
 aut_status launch_generate(int32_t kind, uint64_t seed, int32_t vector_id,
                            uint64_t first, uint64_t n, double *out,
                            cudaStream_t stream);
+aut_status launch_generate_dot_v1(int32_t family, uint64_t seed, int32_t parameter,
+                                  int32_t vector_id, uint64_t count, uint64_t first,
+                                  uint64_t n, float *out, cudaStream_t stream);
 
 } // namespace aut::lib
 
@@ -622,7 +657,7 @@ aut_status aut_dot_variant(aut_workspace *ws, int32_t format, int32_t layout,
   if (st != AUT_OK) return st;
   if (strategy < AUT_STRATEGY_AUTO || strategy > AUT_STRATEGY_SCALAR)
     return fail(AUT_ERR_INVALID_ARGUMENT, "unknown access strategy");
-  if (decoder < AUT_DECODER_AUTO || decoder > AUT_DECODER_EX2_APPROX)
+  if (decoder < AUT_DECODER_AUTO || decoder > AUT_DECODER_SUBNORMAL_LUT)
     return fail(AUT_ERR_INVALID_ARGUMENT, "unknown decoder");
   device_scope scope(ws->device);
   AUT_CUDA_TRY(scope.err);
@@ -663,7 +698,7 @@ aut_status aut_gemv(aut_workspace *ws, int32_t format, int32_t layout,
   if (st != AUT_OK) return st;
   if (strategy < AUT_STRATEGY_AUTO || strategy > AUT_STRATEGY_SCALAR)
     return fail(AUT_ERR_INVALID_ARGUMENT, "unknown access strategy");
-  if (decoder < AUT_DECODER_AUTO || decoder > AUT_DECODER_EX2_APPROX)
+  if (decoder < AUT_DECODER_AUTO || decoder > AUT_DECODER_SUBNORMAL_LUT)
     return fail(AUT_ERR_INVALID_ARGUMENT, "unknown decoder");
   if (rows == 0) return AUT_OK;
   if (rows > 0xffffffffull)
@@ -736,6 +771,23 @@ aut_status aut_generate(int32_t kind, uint64_t seed, int32_t vector_id,
   if (n > 0 && out == nullptr) return fail(AUT_ERR_INVALID_ARGUMENT, "out is NULL");
   return launch_generate(kind, seed, vector_id, first, n, out,
                          static_cast<cudaStream_t>(stream));
+}
+
+aut_status aut_generate_dot_v1(int32_t family, uint64_t seed, int32_t parameter,
+                               int32_t vector_id, uint64_t count, uint64_t first,
+                               uint64_t n, float *out, void *stream) {
+  clear_error();
+  if (family < 0 || family > 3)
+    return fail(AUT_ERR_INVALID_ARGUMENT, "unknown dataset family");
+  if (vector_id != 0 && vector_id != 1)
+    return fail(AUT_ERR_INVALID_ARGUMENT, "vector_id must be 0 (x) or 1 (y)");
+  if (parameter < 0 || parameter > 126)
+    return fail(AUT_ERR_INVALID_ARGUMENT, "parameter must lie in [0, 126]");
+  if (first > count || n > count - first)
+    return fail(AUT_ERR_INVALID_ARGUMENT, "[first, first + n) beyond the case's count");
+  if (n > 0 && out == nullptr) return fail(AUT_ERR_INVALID_ARGUMENT, "out is NULL");
+  return launch_generate_dot_v1(family, seed, parameter, vector_id, count, first, n, out,
+                                static_cast<cudaStream_t>(stream));
 }
 
 aut_status aut_encode_host(int32_t format, const double *values, uint64_t n,

@@ -110,6 +110,8 @@ def parse():
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="e8-sweep")
     p.add_argument("--accum", choices=["fp32", "fp64"], default="fp32")
     p.add_argument("--strategy", choices=["auto", "ldg", "tma"], default="auto")
+    p.add_argument("--layout", choices=["dense", "padded"], default="dense",
+                   help="storage layout of the DOT workloads")
     p.add_argument("--n", type=int, default=0, help="values per GPU (default: workload's)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-per-config", action="store_true",
@@ -354,7 +356,7 @@ def config_of(args, world, desc, n_full):
                 "parallelism": f"rows sharded x{world}, no collective"}
     return {"workload": f"{desc}; N={n} per GPU", "n_per_gpu": n,
             "formats": [f for f, _ in WORKLOADS[args.workload][1]],
-            "layout": "dense", "accumulator": args.accum,
+            "layout": args.layout, "accumulator": args.accum,
             "l2": "inputs larger than L2 (every pair > 126 MB; consecutive DOTs read different buffers)",
             "parallelism": f"contiguous shards x{world}, one FP64 all-reduce per step"}
 
@@ -461,6 +463,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     desc, fmts, layout, n_full = WORKLOADS[args.workload]
+    if args.layout == "padded" and args.workload != "gemv":
+        layout = PADDED
     n = args.n or n_full
     accum = _lib.ACC_FP32 if args.accum == "fp32" else _lib.ACC_FP64
     if any(f == "fp64" for f, _ in fmts):
@@ -671,7 +675,8 @@ def main():
             xw = x.cpu().numpy().view(np.uint32)
             yw = y.cpu().numpy().view(np.uint32)
             bits = _lib.format_info(fids[k])[1]
-            stride = 64 if name == "fp64" else bits
+            stride = 64 if name == "fp64" else (
+                bits if layout == DENSE else (8 if bits <= 8 else 16 if bits <= 16 else 32))
             row_words = cols * stride // 32
             worst = 0.0
             for r in range(sample_rows):

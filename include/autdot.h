@@ -99,11 +99,16 @@ enum {
                                          pair: multiply_kind::fused (lns16_r11) */
   AUT_DECODER_FUSED_SUM_LUT = 5, /* logs added, one lookup per pair in a table of
                                    every product: fused_sum_lut_shared (lns8_r3) */
-  AUT_DECODER_EX2_APPROX = 6    /* logs added, one hardware ex2.approx.f32 per
+  AUT_DECODER_EX2_APPROX = 6,   /* logs added, one hardware ex2.approx.f32 per
                                    pair (ex2_approx with the fused multiply,
                                    lns_decoder_strategies.cuh:215-224; lns8_r3,
                                    lns16_r11).  APPROXIMATE: relative error up to
                                    2^-21 per product; never chosen by AUTO */
+  AUT_DECODER_PREFIX_LUT = 7,   /* sign+exponent table, mantissa ORed in:
+                                   prefix_lut_shared (e8m1, e8m3, e8m5) */
+  AUT_DECODER_SUBNORMAL_LUT = 8 /* table of the subnormal values, bit moves for
+                                   the rest: subnormal_lut_shared (e8m1, e8m3,
+                                   e8m5) */
 };
 
 /* Sticky device status bits reported by aut_workspace_status(). */
@@ -304,6 +309,14 @@ aut_status aut_encode(aut_workspace *ws, int32_t format, int32_t layout,
 /* out[i] = generator value of index first + i. */
 aut_status aut_generate(int32_t kind, uint64_t seed, int32_t vector_id,
                         uint64_t first, uint64_t n, double *out, void *stream);
+/* out[i] = value first + i of vector `vector_id` (0: x, 1: y) of a dot_v1
+ * validation case of `count` values: family 0 positive_uniform, 1
+ * signed_uniform, 2 controlled_cancellation, 3 dynamic_range, with its seed
+ * and parameter (aut::dataset::accuracy_cases), FP32, bit-identical to the
+ * reference's generator (dot_dataset.hpp:72-152). */
+aut_status aut_generate_dot_v1(int32_t family, uint64_t seed, int32_t parameter,
+                               int32_t vector_id, uint64_t count, uint64_t first,
+                               uint64_t n, float *out, void *stream);
 
 /* ---- host codecs (the host half of storage::encode/decode) -------------- */
 aut_status aut_encode_host(int32_t format, const double *values, uint64_t n,

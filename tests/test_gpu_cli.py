@@ -43,7 +43,7 @@ DOT_BENCH_HEADER = (
 def test_tools_are_built_and_answer_help(autlib):
     from accessor_universal_test_b200 import build
     build.build_tools()
-    for tool in ("strategy_bench", "dot_bench"):
+    for tool in ("strategy_bench", "dot_bench", "accessor_dot_bench"):
         r = subprocess.run([os.path.join(LIB, tool), "--help"], capture_output=True, text=True)
         assert r.returncode == 0 and "--output" in r.stdout
 
@@ -109,3 +109,75 @@ def test_dot_bench_accuracy_rows(tmp_path, autlib):
             assert err <= 1e-14, row
         if row["operation"] == "aut_dot_acc32":
             assert err <= 2e-6, row
+
+
+ACCESSOR_ACCURACY_HEADER = (
+    "gpu,compute_capability,multiprocessors,cuda_runtime,cuda_driver,"
+    "dataset,variant,storage_type,arithmetic_type,access_kind,n,blocks,"
+    "threads,result,result_bits,reference,absolute_error,relative_error,"
+    "normalized_error,dot_condition_number,x_fingerprint,"
+    "y_fingerprint,finite")
+
+
+@pytest.mark.gpu
+def test_accessor_dot_bench_accuracy_rows_match_the_golden_dataset(autlib, tmp_path):
+    """accessor_dot_bench --mode accuracy: the reference's schema, the dot_v1
+    fingerprints and reference DOTs of the reference's inspector (golden CSV),
+    and errors no worse than those the reference's own kernels published."""
+    from conftest import GOLDEN
+    out = tmp_path / "accuracy.csv"
+    r = subprocess.run([os.path.join(LIB, "accessor_dot_bench"), "--mode", "accuracy",
+                        "--warmup", "1", "--output", str(out)],
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr
+    text = out.read_text().splitlines()
+    assert text[0] == ACCESSOR_ACCURACY_HEADER
+    rows = list(csv.DictReader(text))
+    assert len(rows) == 9 * 3 * 4
+    with open(os.path.join(GOLDEN, "dot_v1_inspect.csv")) as f:
+        golden = {(g["dataset"], g["n"]): g for g in csv.DictReader(f)}
+    with open(os.path.join(GOLDEN, "accessor_dot_accuracy.csv")) as f:
+        published = {(g["dataset"], g["n"]): g for g in csv.DictReader(f)}
+    for row in rows:
+        g = golden[(row["dataset"], row["n"])]
+        assert row["x_fingerprint"] == g["x_fingerprint"]
+        assert row["y_fingerprint"] == g["y_fingerprint"]
+        assert abs(float(row["reference"]) - float(g["dot_reference"])) <= \
+            1e-15 * max(1.0, abs(float(g["dot_reference"])))
+        assert row["finite"] == "true"
+        theirs = float(published[(row["dataset"], row["n"])][
+            f"{row['variant']}_normalized_error"])
+        assert float(row["normalized_error"]) <= theirs * (1 + 1e-9) + 1e-300, row
+
+
+@pytest.mark.gpu
+def test_device_dot_v1_generator_matches_the_golden_fingerprints(autlib):
+    import numpy as np
+    import torch
+    from conftest import GOLDEN
+    from accessor_universal_test_b200 import _lib
+    cases = {"positive_uniform": (0, 0x123456789ABCDEF0, 0),
+             "signed_uniform_seed0": (1, 0x123456789ABCDEF0, 0),
+             "cancellation_1e6": (2, 0x123456789ABCDEF0, 19),
+             "dynamic_range_40": (3, 0xA4093822299F31D0, 20)}
+    with open(os.path.join(GOLDEN, "dot_v1_inspect.csv")) as f:
+        golden = list(csv.DictReader(f))
+
+    def fnv(a):
+        h = 1469598103934665603
+        for w in a.view(np.uint32).tolist():
+            h = ((h ^ w) * 1099511628211) & 0xFFFFFFFFFFFFFFFF
+        return f"0x{h:x}"
+    for g in golden:
+        if g["dataset"] not in cases or int(g["n"]) > 65536:
+            continue
+        fam, seed, param = cases[g["dataset"]]
+        n = int(g["n"])
+        for vid, key in ((0, "x_fingerprint"), (1, "y_fingerprint")):
+            out = torch.empty(n, dtype=torch.float32, device="cuda")
+            # two halves generated separately: `first` indexes into the case
+            _lib.generate_dot_v1(fam, seed, param, vid, n, out.data_ptr(), 0, n // 2)
+            _lib.generate_dot_v1(fam, seed, param, vid, n, out.data_ptr() + 4 * (n // 2),
+                                 n // 2, n - n // 2)
+            torch.cuda.synchronize()
+            assert fnv(out.cpu().numpy()) == g[key], (g["dataset"], n, vid)

@@ -42,7 +42,9 @@ DECODER_CASES = [("lns8_r3", 0, 2), ("lns8_r3", 1, 2), ("lns8_r3", 0, 5), ("lns8
                  ("lns16_r11", 0, 3), ("lns16_r11", 1, 3), ("lns16_r11", 0, 4),
                  ("lns16_r11", 1, 4), ("e8m5", 0, 1), ("e2m3", 1, 1), ("fp32", 0, 1),
                  ("e2m3", 0, 2), ("e2m3", 1, 2), ("e8m0", 0, 2), ("e8m0", 1, 2),
-                 ("e8m1", 0, 2), ("e8m3", 1, 2), ("e8m5", 0, 2), ("e8m5", 1, 2)]
+                 ("e8m1", 0, 2), ("e8m3", 1, 2), ("e8m5", 0, 2), ("e8m5", 1, 2),
+                 ("e8m1", 0, 7), ("e8m1", 1, 7), ("e8m3", 0, 7), ("e8m5", 1, 7),
+                 ("e8m1", 0, 8), ("e8m3", 1, 8), ("e8m5", 0, 8), ("e8m5", 1, 8)]
 
 
 @pytest.mark.parametrize("name,accum,decoder", DECODER_CASES)
@@ -83,7 +85,9 @@ def test_decoders_without_a_kernel_are_refused(ws):
                ("lns8_r3", 0, 4), ("lns8_r3", 0, 1), ("e8m15", 0, 2), ("bf16_e8m7", 1, 2),
                ("fp32", 0, 2), ("e8m0", 0, 3), ("fp32", 0, 3),
                ("e8m15", 1, 4), ("lns16_r11", 0, 5), ("e8m0", 0, 5), ("fp64", 1, 5),
-               ("e8m0", 0, 6), ("e2m3", 1, 6), ("fp32", 1, 6)]
+               ("e8m0", 0, 6), ("e2m3", 1, 6), ("fp32", 1, 6),
+               ("e8m0", 0, 7), ("e8m15", 0, 7), ("lns8_r3", 0, 7), ("e8m0", 1, 8),
+               ("bf16_e8m7", 0, 8), ("e2m3", 0, 8)]
     for name, accum, decoder in refused:
         with pytest.raises(_lib.AutError) as info:
             ws.dot(_lib.format_id(name), 0, accum, x.data_ptr(), x.data_ptr(), 64,
@@ -91,7 +95,7 @@ def test_decoders_without_a_kernel_are_refused(ws):
         assert info.value.status == _lib.AUT_ERR_UNSUPPORTED, (name, accum, decoder)
     with pytest.raises(_lib.AutError) as info:
         ws.dot(_lib.format_id("e8m0"), 0, 0, x.data_ptr(), x.data_ptr(), 64,
-               res.data_ptr(), decoder=7)
+               res.data_ptr(), decoder=9)
     assert info.value.status == _lib.AUT_ERR_INVALID_ARGUMENT
 
 
@@ -270,3 +274,21 @@ def test_batched_dots_match_single_dots(ws, orc, name):
         ref_dot, ref_abs = oracle_dot(orc, name, n, seed=SEED + b)
         assert normalized_error(got[b], ref_dot, ref_abs) <= TOL[1], (b, got[b], singles[b][0])
         assert abs(got[b] - singles[b][0]) <= 2 * TOL[1] * float(ref_abs)
+
+
+@pytest.mark.parametrize("name", ["e8m1", "e8m3", "e8m5"])
+@pytest.mark.parametrize("layout", [0, 1])
+@pytest.mark.parametrize("decoder", [7, 8])
+def test_partial_table_decoders_in_both_layouts(ws, orc, name, layout, decoder):
+    """prefix_lut / subnormal_lut: exact decodes, so the DOT is within the
+    accumulator's bound in both layouts; inputs with subnormal and special
+    codes run through tests/test_gpu_codec.py's decode checks."""
+    for n in (5, 4099, (1 << 20) + 37):
+        x, y = device_pair(ws, name, layout, n)
+        ref_dot, ref_abs = oracle_dot(orc, name, n)
+        for accum in (0, 1):
+            for strategy in (1, 2):
+                got = gpu_dot(ws, name, layout, accum, x, y, n, strategy=strategy,
+                              decoder=decoder)
+                err = normalized_error(got, ref_dot, ref_abs)
+                assert err <= TOL[accum], (name, layout, decoder, accum, n, got, float(err))

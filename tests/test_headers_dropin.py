@@ -32,6 +32,23 @@ def test_reference_unit_test_compiles_and_passes_against_include(name, tmp_path)
     assert run.returncode == 0, (run.stdout[-2000:], run.stderr[-2000:])
 
 
+def test_reference_inspector_reproduces_the_golden_csv(tmp_path):
+    """The reference's own dataset inspector (tools/inspect_dot_dataset.cpp)
+    built against include/dot_dataset.hpp prints the golden CSV that the
+    reference's build of it printed."""
+    src = os.path.join(REF, "tools", "inspect_dot_dataset.cpp")
+    if not os.path.exists(src):
+        pytest.skip("reference tree not available on this machine")
+    exe = str(tmp_path / "inspect")
+    build = subprocess.run(["g++", "-O3", "-std=c++17", "-I", os.path.join(ROOT, "include"),
+                            src, "-o", exe], capture_output=True, text=True)
+    assert build.returncode == 0, build.stderr[-4000:]
+    out = subprocess.run([exe, "1024", "65536", "1048576"], capture_output=True, text=True,
+                         timeout=300).stdout
+    with open(os.path.join(ROOT, "tests", "golden", "dot_v1_inspect.csv")) as f:
+        assert out == f.read()
+
+
 def test_headers_compile_for_the_device():
     """The same headers inside a CUDA translation unit for sm_100a."""
     nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
@@ -43,6 +60,7 @@ def test_headers_compile_for_the_device():
 #include "decoder_strategy_core.hpp"
 #include "bitwidth_benchmark_core.hpp"
 #include "lns_benchmark_core.hpp"
+#include "dot_dataset.hpp"
 namespace bw = aut::bitwidth;
 __global__ void k(const unsigned *in, double *out, float *out32) {
   const unsigned r = in[threadIdx.x];
