@@ -25,7 +25,7 @@ FAMILY_BINARY, FAMILY_PREFIX, FAMILY_LNS, FAMILY_RAW_FP32, FAMILY_RAW_FP64 = ran
 DENSE, PADDED = 0, 1
 ACC_FP32, ACC_FP64 = 0, 1
 TARGET_FP32, TARGET_FP64 = 0, 1
-STRATEGY_AUTO, STRATEGY_LDG, STRATEGY_TMA, STRATEGY_SCALAR = 0, 1, 2, 3
+STRATEGY_AUTO, STRATEGY_LDG, STRATEGY_TMA, STRATEGY_SCALAR, STRATEGY_COOPERATIVE = 0, 1, 2, 3, 4
 (DECODER_AUTO, DECODER_DIRECT, DECODER_FULL_LUT, DECODER_FRACTION_LUT,
  DECODER_FRACTION_LUT_FUSED, DECODER_FUSED_SUM_LUT, DECODER_EX2_APPROX,
  DECODER_PREFIX_LUT, DECODER_SUBNORMAL_LUT) = range(9)

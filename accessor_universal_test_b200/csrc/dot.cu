@@ -19,6 +19,8 @@
 #include "dot_device.cuh"
 #include "internal.hpp"
 
+#include "aut/bitwidth.hpp"
+
 #include <cuda_fp16.h>
 
 #include <cstdio>
@@ -105,7 +107,7 @@ template <int S, int W> struct e8_codec {
           const float p = __uint_as_float(field_top<S, W>(xw, v)) *
                           __uint_as_float(field_top<S, W>(yw, v));
           smallest = fminf(smallest, fabsf(p));
-          if (v & 1)
+          if (v & 2)  // adjacent values share a chain (see acc_f32)
             s1 += static_cast<double>(p);
           else
             s0 += static_cast<double>(p);
@@ -1167,6 +1169,103 @@ __device__ __forceinline__ void ragged_tail(const unsigned char *xb, uint64_t xo
 }
 
 // ---------------------------------------------------------------------------
+// COOPERATIVE strategy: the reference's cooperative shuffle loader
+// (cooperative_raw / dot_cooperative_kernel, bitwidth_benchmark_kernels.cuh:
+// 503-572; geometry bitwidth_benchmark_core.hpp:87-121) for dense streams.
+// A group of `consumers` lanes owns one aligned chunk of `values` codes that
+// spans `words` words: the first `words` lanes load one word each (a warp's
+// loads are consecutive words), every lane then fetches the two words its
+// codes lie in by two warp shuffles (the group's spare lanes hold 0 and
+// serve as the guard word) and extracts values / consumers codes from the
+// 64-bit pair.  Values past the last whole chunk take the per-value path.
+// It reads every word once from global memory and never from shared memory;
+// it stays behind the bulk-copy ring on B200 (shuffles and per-code shifts),
+// kept for the access-method axis, never chosen by AUTO.
+// ---------------------------------------------------------------------------
+template <int W> struct coop_e8 {  // IEEE-like code with an 8-bit exponent
+  __device__ __forceinline__ static float value(uint32_t c) {
+    return __uint_as_float(c << (32 - W));
+  }
+};
+struct coop_e2m3 {
+  __device__ __forceinline__ static float value(uint32_t c) {
+    uint32_t h2;
+    asm("cvt.rn.f16x2.e2m3x2 %0, %1;" : "=r"(h2) : "h"(static_cast<unsigned short>(c & 0x3fu)));
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(h2)));
+  }
+};
+
+template <int B, class Dec, class Acc>
+__global__ void __launch_bounds__(kThreads) dot_coop_kernel(const dot_params p) {
+  __shared__ double scratch[kScratchDoubles];
+  using geo = aut::bitwidth::cooperative_geometry<B>;
+  constexpr int C = geo::consumers;
+  constexpr int WORDS = geo::words;
+  constexpr int VALS = geo::values;
+  constexpr int VPC = geo::values_per_consumer;
+  constexpr int GROUPS = 32 / C;  // chunks per warp and step
+  static_assert(VPC * B <= 32, "a consumer's codes lie in two words");
+  constexpr uint32_t kMask = B == 32 ? 0xffffffffu : (1u << B) - 1u;
+
+  const unsigned int batch = blockIdx.y;
+  const unsigned char *xb = p.x + batch * p.x_stride;
+  const unsigned char *yb = p.y + batch * p.y_stride;
+  const uint64_t xo = p.x_first + batch * p.x_index_stride;
+  const uint64_t yo = p.y_first + batch * p.y_index_stride;
+  const uint32_t *xw = reinterpret_cast<const uint32_t *>(xb);
+  const uint32_t *yw = reinterpret_cast<const uint32_t *>(yb);
+
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t g = lane / C, c = lane % C;
+  const uint32_t bit0 = c * VPC * B;
+  const uint32_t src = g * C + (bit0 >> 5);  // lane holding the first word
+  const uint32_t sh = bit0 & 31u;
+  const uint64_t chunks = p.vector_ok ? p.n / VALS : 0;
+  const uint64_t warp = (static_cast<uint64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+  const uint64_t step = (static_cast<uint64_t>(gridDim.x) * kThreads >> 5) * GROUPS;
+
+  Acc acc;
+  int since_flush = 0;
+  // the loop bound is the same for all lanes of a warp (shuffles need them all)
+  for (uint64_t base = warp * GROUPS; base < chunks; base += step) {
+    const uint64_t chunk = base + g;
+    const bool live = chunk < chunks;
+    uint32_t wx = 0u, wy = 0u;
+    if (live && c < static_cast<uint32_t>(WORDS)) {
+      wx = __ldg(xw + chunk * WORDS + c);
+      wy = __ldg(yw + chunk * WORDS + c);
+    }
+    const uint32_t x0 = __shfl_sync(0xffffffffu, wx, src);
+    const uint32_t x1 = __shfl_sync(0xffffffffu, wx, src + 1);
+    const uint32_t y0 = __shfl_sync(0xffffffffu, wy, src);
+    const uint32_t y1 = __shfl_sync(0xffffffffu, wy, src + 1);
+    if (live) {
+      const uint64_t px = ((static_cast<uint64_t>(x1) << 32) | x0) >> sh;
+      const uint64_t py = ((static_cast<uint64_t>(y1) << 32) | y0) >> sh;
+#pragma unroll
+      for (int v = 0; v < VPC; ++v)
+        acc.mac(v, Dec::value(static_cast<uint32_t>(px >> (v * B)) & kMask),
+                Dec::value(static_cast<uint32_t>(py >> (v * B)) & kMask));
+    }
+    if (++since_flush == 32 / VPC) {  // at most 32 products per FP32 chain
+      acc.flush();
+      since_flush = 0;
+    }
+  }
+  acc.flush();
+  // values past the whole chunks (or every value of an unaligned stream)
+  for (uint64_t i = chunks * VALS + static_cast<uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
+       i < p.n; i += static_cast<uint64_t>(gridDim.x) * kThreads) {
+    const float a = Dec::value(load_code<B, B>(xb, xo + i));
+    const float b = Dec::value(load_code<B, B>(yb, yo + i));
+    acc.mac_d(0, static_cast<double>(a), static_cast<double>(b));
+  }
+  const dd s = block_sum_dd(acc.pair(), scratch);
+  grid_finish_dd(s, p.partials + 2 * static_cast<uint64_t>(batch) * gridDim.x,
+                 p.tickets + batch, p.results + batch, scratch);
+}
+
+// ---------------------------------------------------------------------------
 // LDG strategy: packets of Q 16-byte vectors straight into registers.
 // ---------------------------------------------------------------------------
 template <class Codec, class Acc>
@@ -1243,7 +1342,7 @@ constexpr int tma_group(int uw) {
 }
 constexpr int tma_vpt(int s) {
   const int uw = s / gcd_int(s, 32), uv = s == 64 ? 1 : 32 / gcd_int(s, 32);
-  const int base = s >= 24 ? 16 : (s <= 4 ? 128 : 32);
+  const int base = s >= 24 ? 16 : (s <= 4 ? 128 : (s == 8 ? 64 : 32));
   return base >= tma_group(uw) * uv ? base : tma_group(uw) * uv;
 }
 
@@ -1280,7 +1379,7 @@ struct tma_shape {
 // warps instead (e8m0 5751 at 64 KiB, 4748 at 160; halving e8m0's tile to 32
 // codes per thread: 5457 at 64 KiB, 5104 at 96).
 constexpr int tma_ring(int s, bool fp64) {
-  if (fp64) return 64 * 1024;
+  if (fp64) return s == 24 ? 128 * 1024 : 64 * 1024;  // 24 bits: e8m15 6368 -> 6649
   return s == 9 || s == 14 ? 160 * 1024 : (s == 10 || s == 12 || s == 24 ? 128 * 1024 : 64 * 1024);
 }
 
@@ -1979,6 +2078,35 @@ int auto_strategy(int32_t format, int32_t layout, int32_t accum) {
   }
 }
 
+template <int B, class Dec>
+kernel_entry coop_entry(int32_t accum) {
+  using namespace aut::dev;
+  kernel_entry e;
+  e.stride = B;
+  e.fn = accum == AUT_ACCUM_FP32 ? dot_coop_kernel<B, Dec, acc_f32> : dot_coop_kernel<B, Dec, acc_f64>;
+  e.smem = 0;
+  using geo = aut::bitwidth::cooperative_geometry<B>;
+  e.tile_values = static_cast<uint64_t>(kThreads / geo::consumers) * geo::values;
+  return e;
+}
+
+// The cooperative shuffle loader: dense E8 and e2m3 streams, decoded by
+// bit moves / the hardware conversion.
+kernel_entry coop_lookup(int32_t format, int32_t layout, int32_t accum) {
+  using namespace aut::dev;
+  if (layout != AUT_LAYOUT_DENSE) return {};
+  switch (format) {
+  case AUT_FMT_E2M3: return coop_entry<6, coop_e2m3>(accum);
+  case AUT_FMT_E8M0: return coop_entry<9, coop_e8<9>>(accum);
+  case AUT_FMT_E8M1: return coop_entry<10, coop_e8<10>>(accum);
+  case AUT_FMT_E8M3: return coop_entry<12, coop_e8<12>>(accum);
+  case AUT_FMT_E8M5: return coop_entry<14, coop_e8<14>>(accum);
+  case AUT_FMT_BF16_E8M7: return coop_entry<16, coop_e8<16>>(accum);
+  case AUT_FMT_E8M15: return coop_entry<24, coop_e8<24>>(accum);
+  default: return {};
+  }
+}
+
 // Decoders per format (the reference's decoder_kind axis): the E8 formats,
 // raw storage and e2m3 decode DIRECT (bit moves / hardware conversion);
 // lns8_r3 has FULL_LUT and FUSED_SUM_LUT; lns16_r11 has FULL_LUT (FP32
@@ -2041,14 +2169,10 @@ kernel_entry lookup(int32_t format, int32_t layout, int32_t accum, int strategy,
     // never chosen by AUTO: approximate
     if (format == AUT_FMT_LNS8_R3)
       return accum == AUT_ACCUM_FP32 ? make_entry<lns_ex2_codec<8, float>, acc_f32>(s, 0)
-                                     : make_entry<lns_ex2_codec<8, double>, acc_f64c>(s, 0);
+                                     : make_entry<lns_ex2_codec<8, double>, acc_f64>(s, 0);
     return accum == AUT_ACCUM_FP32 ? make_entry<lns_ex2_codec<16, float>, acc_f32>(s, 0)
-                                   : make_entry<lns_ex2_codec<16, double>, acc_f64c>(s, 0);
+                                   : make_entry<lns_ex2_codec<16, double>, acc_f64>(s, 0);
   }
-  // LNS with the FP64 accumulator: products of two table values round, and
-  // on data whose signs alternate the two FMA chains of acc_f64 would each
-  // collect one sign; acc_f64c keeps every product's and every addition's
-  // rounding error instead.
   if (format == AUT_FMT_LNS16_R11) {
     const bool f32 = accum == AUT_ACCUM_FP32;
     switch (decoder) {
@@ -2057,10 +2181,10 @@ kernel_entry lookup(int32_t format, int32_t layout, int32_t accum, int strategy,
       return make_entry<lns16_full_codec, acc_f32>(s, 1);
     case AUT_DECODER_FRACTION_LUT:
       return f32 ? make_entry<lns16_codec<float>, acc_f32>(s, 3)
-                 : make_entry<lns16_codec<double>, acc_f64c>(s, 4);
+                 : make_entry<lns16_codec<double>, acc_f64>(s, 4);
     default:  // AUTO, FRACTION_LUT_FUSED
       return f32 ? make_entry<lns16_fused_codec<float>, acc_f32>(s, 3)
-                 : make_entry<lns16_fused_codec<double>, acc_f64c>(s, 4);
+                 : make_entry<lns16_fused_codec<double>, acc_f64>(s, 4);
     }
   }
   switch (format) {
@@ -2083,18 +2207,18 @@ kernel_entry lookup(int32_t format, int32_t layout, int32_t accum, int strategy,
     return dense ? pick<e8_codec<14, 14>>(s, accum, 0) : pick<e8_codec<16, 14>>(s, accum, 0);
   case AUT_FMT_BF16_E8M7: return pick<e8_codec<16, 16>>(s, accum, 0);
   case AUT_FMT_E8M15:
-    // 16-bit significands: FP32 products round, so the FP32 accumulator is
-    // compensated (acc_f32c); the bulk copies keep the kernel HBM-bound
-    if (accum == AUT_ACCUM_FP32)
-      return dense ? make_entry<e8_codec<24, 24>, acc_f32c>(s, 0)
-                   : make_entry<e8_codec<32, 24>, acc_f32c>(s, 0);
-    return dense ? pick<e8_codec<24, 24>>(s, accum, 0) : pick<e8_codec<32, 24>>(s, accum, 0);
+    // 16-bit significands: an FP32 product rounds, so both accumulators
+    // widen the operands and sum the exact products in FP64 (FP32 chains:
+    // normalised error 7.7e-12 at 2^27; FP64: 2.8e-21, and the bulk-copy
+    // kernel stays HBM-bound either way, 6644 GB/s against 6802 for FP32)
+    return dense ? make_entry<e8_codec<24, 24>, acc_f64>(s, 0)
+                 : make_entry<e8_codec<32, 24>, acc_f64>(s, 0);
   case AUT_FMT_LNS8_R3:
     if (decoder == AUT_DECODER_FUSED_SUM_LUT)
       return accum == AUT_ACCUM_FP32 ? make_entry<lns8_fused_codec<float>, acc_f32>(s, 5)
-                                     : make_entry<lns8_fused_codec<double>, acc_f64c>(s, 6);
+                                     : make_entry<lns8_fused_codec<double>, acc_f64>(s, 6);
     return accum == AUT_ACCUM_FP32 ? make_entry<lns8_codec<float>, acc_f32>(s, 1)
-                                   : make_entry<lns8_codec<double>, acc_f64c>(s, 2);
+                                   : make_entry<lns8_codec<double>, acc_f64>(s, 2);
   default: return {};
   }
 }
@@ -2216,8 +2340,12 @@ aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
                               static_cast<cudaStream_t>(stream), partials, tickets,
                               max_blocks_total);
   }
-  kernel_entry e = lookup(format, layout, accum,
-                          scalar_only ? AUT_STRATEGY_LDG : strategy, decoder);
+  const bool coop = strategy == AUT_STRATEGY_COOPERATIVE;
+  if (coop && decoder != AUT_DECODER_AUTO && decoder != AUT_DECODER_DIRECT)
+    return fail(AUT_ERR_UNSUPPORTED, "the cooperative loader decodes by bit moves (DIRECT)");
+  kernel_entry e = coop ? coop_lookup(format, layout, accum)
+                        : lookup(format, layout, accum,
+                                 scalar_only ? AUT_STRATEGY_LDG : strategy, decoder);
   if (e.fn == nullptr)
     return fail(AUT_ERR_UNSUPPORTED,
                 "no fused DOT kernel for this format/layout/accumulator/decoder");

@@ -189,11 +189,17 @@ struct acc_f32c {
 // without rounding for the double-double reductions.
 struct acc_f64 {
   double a[2] = {0.0, 0.0};
+  // Values 2k and 2k + 1 share a chain (chain k mod 2): on data whose signs
+  // alternate from value to value (the LNS cancellation pair) each chain's
+  // partial sum then cancels as it goes instead of growing with one sign,
+  // which keeps its rounding errors small (lns8_r3, N = 2^28: normalised
+  // error 6.6e-19 -> 4.8e-20).
   __device__ __forceinline__ void mac(int slot, float x, float y) {
-    a[slot & 1] = fma(static_cast<double>(x), static_cast<double>(y), a[slot & 1]);
+    a[(slot >> 1) & 1] =
+        fma(static_cast<double>(x), static_cast<double>(y), a[(slot >> 1) & 1]);
   }
   __device__ __forceinline__ void mac_d(int slot, double x, double y) {
-    a[slot & 1] = fma(x, y, a[slot & 1]);
+    a[(slot >> 1) & 1] = fma(x, y, a[(slot >> 1) & 1]);
   }
   __device__ __forceinline__ void add_exact(double v) { a[0] += v; }
   __device__ __forceinline__ void flush() {}

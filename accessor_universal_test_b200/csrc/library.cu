@@ -655,7 +655,7 @@ aut_status aut_dot_variant(aut_workspace *ws, int32_t format, int32_t layout,
   clear_error();
   aut_status st = check_dot_args(ws, format, layout, accum, x, y, n, result);
   if (st != AUT_OK) return st;
-  if (strategy < AUT_STRATEGY_AUTO || strategy > AUT_STRATEGY_SCALAR)
+  if (strategy < AUT_STRATEGY_AUTO || strategy > AUT_STRATEGY_COOPERATIVE)
     return fail(AUT_ERR_INVALID_ARGUMENT, "unknown access strategy");
   if (decoder < AUT_DECODER_AUTO || decoder > AUT_DECODER_SUBNORMAL_LUT)
     return fail(AUT_ERR_INVALID_ARGUMENT, "unknown decoder");
@@ -696,7 +696,7 @@ aut_status aut_gemv(aut_workspace *ws, int32_t format, int32_t layout,
   aut_status st = check_dot_args(ws, format, layout, accum, matrix, vector,
                                  rows == 0 ? 0 : columns, result);
   if (st != AUT_OK) return st;
-  if (strategy < AUT_STRATEGY_AUTO || strategy > AUT_STRATEGY_SCALAR)
+  if (strategy < AUT_STRATEGY_AUTO || strategy > AUT_STRATEGY_COOPERATIVE)
     return fail(AUT_ERR_INVALID_ARGUMENT, "unknown access strategy");
   if (decoder < AUT_DECODER_AUTO || decoder > AUT_DECODER_SUBNORMAL_LUT)
     return fail(AUT_ERR_INVALID_ARGUMENT, "unknown decoder");

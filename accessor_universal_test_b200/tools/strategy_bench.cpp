@@ -189,13 +189,15 @@ std::vector<decoder_choice> decoders_for(const std::string &fmt, int32_t accum) 
   }
   if (fmt == "lns8_r3")
     return {{AUT_DECODER_FULL_LUT, "full_lut_shared", "ordinary", 256 * 32 * t},
-            {AUT_DECODER_FUSED_SUM_LUT, "fused_sum_lut_shared", "fused", 256 * 32 * t}};
+            {AUT_DECODER_FUSED_SUM_LUT, "fused_sum_lut_shared", "fused", 256 * 32 * t},
+            {AUT_DECODER_EX2_APPROX, "ex2_approx", "fused", 0}};
   if (fmt == "lns16_r11") {
     std::vector<decoder_choice> d;
     if (accum == AUT_ACCUM_FP32)
       d.push_back({AUT_DECODER_FULL_LUT, "full_lut_shared", "ordinary", 32768 * 4});
     d.push_back({AUT_DECODER_FRACTION_LUT, "fraction_lut_shared", "ordinary", 2048 * t});
     d.push_back({AUT_DECODER_FRACTION_LUT_FUSED, "fraction_lut_shared", "fused", 2048 * t});
+    d.push_back({AUT_DECODER_EX2_APPROX, "ex2_approx", "fused", 0});
     return d;
   }
   if (fmt == "e2m3")
@@ -205,10 +207,32 @@ std::vector<decoder_choice> decoders_for(const std::string &fmt, int32_t accum) 
     const int32_t fid = aut_format_id(fmt.c_str());
     int32_t family = 0, bits = 0, e = 0, fin = 0;
     aut_format_info(fid, &family, &bits, &e, &fin);
-    return {{AUT_DECODER_DIRECT, "direct_shift", "ordinary", 0},
-            {AUT_DECODER_FULL_LUT, "full_lut_shared", "ordinary", (1 << bits) * 4}};
+    std::vector<decoder_choice> d = {{AUT_DECODER_DIRECT, "direct_shift", "ordinary", 0},
+                                     {AUT_DECODER_FULL_LUT, "full_lut_shared", "ordinary",
+                                      (1 << bits) * 4}};
+    if (bits > 9) {  // the partial tables need mantissa bits
+      d.push_back({AUT_DECODER_PREFIX_LUT, "prefix_lut_shared", "ordinary", 512 * 4});
+      d.push_back({AUT_DECODER_SUBNORMAL_LUT, "subnormal_lut_shared", "ordinary",
+                   (1 << (bits - 9)) * 4});
+    }
+    return d;
   }
   return {{AUT_DECODER_DIRECT, "direct_shift", "ordinary", 0}};
+}
+
+// The cooperative loader's chunk (cooperative_geometry of
+// include/aut/bitwidth.hpp, for a runtime width).
+struct coop_geometry {
+  int values, words, consumers;
+};
+coop_geometry coop_geometry_of(int bits) {
+  const int g = gcd_int(bits, 32);
+  coop_geometry c{32 / g, bits / g, 0};
+  int above = 1;
+  while (above <= c.words) above *= 2;
+  c.consumers = std::max({4, above, c.values / 4});
+  c.consumers = std::min(c.consumers, c.values);
+  return c;
 }
 
 } // namespace
@@ -256,7 +280,9 @@ int main(int argc, char **argv) {
 
     const access accesses[] = {{"scalar", AUT_STRATEGY_SCALAR, "none"},
                                {"thread_packet", AUT_STRATEGY_LDG, "none"},
-                               {"tma_bulk", AUT_STRATEGY_TMA, "tma_bulk_shared"}};
+                               {"tma_bulk", AUT_STRATEGY_TMA, "tma_bulk_shared"},
+                               {"cooperative_shuffle", AUT_STRATEGY_COOPERATIVE,
+                                "warp_shuffle"}};
     const int max_power = *std::max_element(o.dot_powers.begin(), o.dot_powers.end());
     uint64_t max_n = uint64_t{1} << max_power;
     for (int p : o.gemv_powers)
@@ -332,9 +358,15 @@ int main(int argc, char **argv) {
                 else
                   csv << name << ',' << bits << ',' << ebits << ',' << (bits - 1 - ebits)
                       << ',' << acc_name << ',';
+                // cooperative rows: chunk values, words (loader lanes),
+                // consumer lanes and values per consumer of the geometry
+                const bool coop = ac.strategy == AUT_STRATEGY_COOPERATIVE;
+                const coop_geometry cg = coop_geometry_of(bits);
                 csv << (layout == AUT_LAYOUT_DENSE ? "dense" : "padded") << ',' << ac.name
-                    << ',' << packet << ',' << (layout == AUT_LAYOUT_DENSE ? 32 : stride)
-                    << ",1," << (ac.strategy == AUT_STRATEGY_TMA ? 256 : 1) << ',' << packet
+                    << ',' << packet << ',' << (layout == AUT_LAYOUT_DENSE ? 32 : stride) << ','
+                    << (coop ? cg.words : 1) << ','
+                    << (coop ? cg.consumers : ac.strategy == AUT_STRATEGY_TMA ? 256 : 1) << ','
+                    << (coop ? cg.values / cg.consumers : packet)
                     << ',' << ac.redistribution << ',' << dc.name << ',' << id << ',' << n
                     << ',' << m << ',' << rows << ',' << logical << ',' << physical << ','
                     << dc.table_bytes << ',' << blocks << ",256," << o.warmup << ',' << k
@@ -351,6 +383,8 @@ int main(int argc, char **argv) {
             for (const access &ac : accesses) {
               const bool scalar = ac.strategy == AUT_STRATEGY_SCALAR;
               const int packet = scalar ? 1
+                                 : ac.strategy == AUT_STRATEGY_COOPERATIVE
+                                     ? coop_geometry_of(bits).values
                                  : ac.strategy == AUT_STRATEGY_LDG
                                      ? 128 * (stride / gcd_int(stride, 128)) / stride
                                      : (stride >= 24 ? 16 : 32);

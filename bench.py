@@ -705,7 +705,8 @@ def main():
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32 products, f64 carry" if accum == _lib.ACC_FP32 else "f64",
+        "dtype": ("fp32 FMA chains of <= 32 products with fp64 carries (e8m15: fp64)"
+                  if accum == _lib.ACC_FP32 else "fp64"),
         "data": "synthetic (seeded splitmix64, generated and encoded on the GPU)",
         "config": config_of(args, world, desc, n_full),
         "decoded_elems_per_s": elems,

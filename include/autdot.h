@@ -83,8 +83,11 @@ enum {
   AUT_STRATEGY_AUTO = 0,
   AUT_STRATEGY_LDG = 1,   /* 16-byte vector loads straight into registers   */
   AUT_STRATEGY_TMA = 2,   /* cp.async.bulk tiles into a shared-memory ring   */
-  AUT_STRATEGY_SCALAR = 3 /* one code per load (the reference's scalar
+  AUT_STRATEGY_SCALAR = 3, /* one code per load (the reference's scalar
                              access method); the slow baseline            */
+  AUT_STRATEGY_COOPERATIVE = 4 /* groups of lanes load a chunk's words once
+                             and share them by warp shuffles
+                             (cooperative_shuffle; dense E8 and e2m3) */
 };
 
 /* How the fused DOT turns codes into values (decoder_kind,

@@ -84,7 +84,10 @@ def test_strategy_bench_smoke_passes_the_reference_validator_rule(tmp_path, autl
     assert lines[0] == (LNS_HEADER if family == "lns" else BITWIDTH_HEADER)
     rows = list(csv.DictReader(lines))
     strategies = {row["access_method"] for row in rows}
-    assert strategies == {"scalar", "thread_packet", "tma_bulk"}
+    expected = {"scalar", "thread_packet", "tma_bulk"}
+    if family == "bitwidth":  # dense E8 / e2m3 streams also take the shuffle loader
+        expected.add("cooperative_shuffle")
+    assert strategies == expected
     _validate(rows, family == "lns")
 
 

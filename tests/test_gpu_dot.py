@@ -292,3 +292,36 @@ def test_partial_table_decoders_in_both_layouts(ws, orc, name, layout, decoder):
                               decoder=decoder)
                 err = normalized_error(got, ref_dot, ref_abs)
                 assert err <= TOL[accum], (name, layout, decoder, accum, n, got, float(err))
+
+
+COOP_FORMATS = ["e2m3", "e8m0", "e8m1", "e8m3", "e8m5", "bf16_e8m7", "e8m15"]
+
+
+@pytest.mark.parametrize("name", COOP_FORMATS)
+def test_cooperative_shuffle_loader_matches_oracle(ws, orc, name):
+    """AUT_STRATEGY_COOPERATIVE (cooperative_shuffle): dense streams, whole
+    chunks through the shuffles and the rest value by value, unaligned
+    streams entirely value by value."""
+    from accessor_universal_test_b200 import _lib
+    for n in SIZES:
+        x, y = device_pair(ws, name, 0, n)
+        ref_dot, ref_abs = oracle_dot(orc, name, n)
+        for accum in (0, 1):
+            got = gpu_dot(ws, name, 0, accum, x, y, n, strategy=_lib.STRATEGY_COOPERATIVE)
+            err = normalized_error(got, ref_dot, ref_abs)
+            assert err <= TOL[accum], (name, accum, n, got, float(ref_dot), float(err))
+            if name == "e2m3":
+                assert got == float(ref_dot), (name, n, got)
+
+
+def test_cooperative_loader_is_refused_where_it_does_not_apply(ws):
+    import torch
+    from accessor_universal_test_b200 import _lib
+    x = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+    res = torch.zeros(1, dtype=torch.float64, device="cuda")
+    for name, layout, decoder in (("lns16_r11", 0, 0), ("fp32", 0, 0), ("e8m0", 1, 0),
+                                  ("e8m0", 0, 2), ("lns8_r3", 0, 0)):
+        with pytest.raises(_lib.AutError) as info:
+            ws.dot(_lib.format_id(name), layout, 0, x.data_ptr(), x.data_ptr(), 64,
+                   res.data_ptr(), strategy=_lib.STRATEGY_COOPERATIVE, decoder=decoder)
+        assert info.value.status == _lib.AUT_ERR_UNSUPPORTED, (name, layout, decoder)
