@@ -61,6 +61,9 @@ struct dot_params {
   uint64_t stall_tile;    // failure-detection test: this tile's stage is
                           // armed but its copies are never issued, so the
                           // wait for it runs out (~0: none)
+  unsigned int *claims;   // [gridDim.y] tile counters of the bulk-copy kernel's
+                          // dynamic tail (order-free codecs), zero between
+                          // launches; nullptr: every tile assigned statically
 };
 
 // ---------------------------------------------------------------------------
@@ -301,7 +304,7 @@ template <typename T> struct lane_table {
     return (threadIdx.x & (kCopies - 1)) * static_cast<uint32_t>(sizeof(T));
   }
   __device__ static void fill(T *s, const T *g, int entries) {
-    for (int e = threadIdx.x; e < entries * kCopies; e += kThreads) s[e] = g[e / kCopies];
+    for (int e = threadIdx.x; e < entries * kCopies; e += blockDim.x) s[e] = g[e / kCopies];
   }
   // entry `code` of this lane's copy
   __device__ __forceinline__ static T at(const unsigned char *smem, uint32_t code,
@@ -480,7 +483,7 @@ template <typename T> struct lns16_codec {
     const void *table = p.table;
     const T *g = static_cast<const T *>(table);
     T *s = reinterpret_cast<T *>(smem);
-    for (int e = threadIdx.x; e < 2048; e += kThreads) s[e] = g[e];
+    for (int e = threadIdx.x; e < 2048; e += blockDim.x) s[e] = g[e];
   }
 
   __device__ __forceinline__ static T decode(uint32_t c, const T *tab) {
@@ -547,7 +550,7 @@ struct lns16_full_codec {
     const void *table = p.table;
     const uint4 *g = static_cast<const uint4 *>(table);
     uint4 *s = reinterpret_cast<uint4 *>(smem);
-    for (int e = threadIdx.x; e < 32768 / 4; e += kThreads) s[e] = g[e];
+    for (int e = threadIdx.x; e < 32768 / 4; e += blockDim.x) s[e] = g[e];
   }
 
   __device__ __forceinline__ static float at(const unsigned char *smem, uint32_t off) {
@@ -642,7 +645,7 @@ template <typename T> struct lns16_fused_codec {
   __device__ static void prepare(const dot_params &p, unsigned char *smem) {
     const T *g = static_cast<const T *>(p.table);
     T *s = reinterpret_cast<T *>(smem);
-    for (int e = threadIdx.x; e < 2048; e += kThreads) s[e] = g[e];
+    for (int e = threadIdx.x; e < 2048; e += blockDim.x) s[e] = g[e];
     if (threadIdx.x == 0) {
       multipliers m{};
       m.one = 1u;
@@ -901,7 +904,7 @@ template <int S, int W, typename T> struct wide_lut_codec {
   __device__ static void prepare(const dot_params &p, unsigned char *smem) {
     const uint4 *g = static_cast<const uint4 *>(p.table);
     uint4 *s = reinterpret_cast<uint4 *>(smem);
-    for (int e = threadIdx.x; e < (1 << W) / 4; e += kThreads) s[e] = g[e];
+    for (int e = threadIdx.x; e < (1 << W) / 4; e += blockDim.x) s[e] = g[e];
   }
 
   __device__ __forceinline__ static T value(uint32_t code, const unsigned char *smem) {
@@ -964,7 +967,7 @@ template <int S, int W, typename T, bool kPrefix> struct part_lut_codec {
   __device__ static void prepare(const dot_params &p, unsigned char *smem) {
     const uint32_t *g = static_cast<const uint32_t *>(p.table);
     uint32_t *t = reinterpret_cast<uint32_t *>(smem);
-    for (int e = threadIdx.x; e < kEntries; e += kThreads) t[e] = g[e];
+    for (int e = threadIdx.x; e < kEntries; e += blockDim.x) t[e] = g[e];
   }
 
   __device__ __forceinline__ static T decode(uint32_t c, const uint32_t *tab) {
@@ -1163,8 +1166,8 @@ __device__ __forceinline__ void ragged_tail(const unsigned char *xb, uint64_t xo
                                             const unsigned char *yb, uint64_t yo,
                                             uint64_t first, uint64_t n,
                                             Acc &acc, const unsigned char *smem) {
-  for (uint64_t i = first + static_cast<uint64_t>(blockIdx.x) * kThreads + threadIdx.x;
-       i < n; i += static_cast<uint64_t>(gridDim.x) * kThreads)
+  for (uint64_t i = first + static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+       i < n; i += static_cast<uint64_t>(gridDim.x) * blockDim.x)
     Codec::scalar(xb, xo + i, yb, yo + i, acc, smem);
 }
 
@@ -1224,6 +1227,8 @@ __global__ void __launch_bounds__(kThreads) dot_coop_kernel(const dot_params p) 
   const uint64_t warp = (static_cast<uint64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
   const uint64_t step = (static_cast<uint64_t>(gridDim.x) * kThreads >> 5) * GROUPS;
 
+  pdl_wait();
+  pdl_release();
   Acc acc;
   int since_flush = 0;
   // the loop bound is the same for all lanes of a warp (shuffles need them all)
@@ -1285,6 +1290,8 @@ __global__ void __launch_bounds__(kThreads)
   const uint64_t xo = p.x_first + batch * p.x_index_stride;
   const uint64_t yo = p.y_first + batch * p.y_index_stride;
 
+  pdl_wait();
+  pdl_release();
   if constexpr (Codec::kTableBytes > 0) {
     Codec::prepare(p, smem);
     __syncthreads();
@@ -1346,8 +1353,9 @@ constexpr int tma_vpt(int s) {
   return base >= tma_group(uw) * uv ? base : tma_group(uw) * uv;
 }
 
-template <int S, int RING = 64 * 1024, int VPT_ = tma_vpt(S)>
+template <int S, int RING = 64 * 1024, int VPT_ = tma_vpt(S), int NT_ = kThreads>
 struct tma_shape {
+  static constexpr int NT = NT_;                   // threads per block
   static constexpr int G = gcd_int(S, 32);
   static constexpr int UW = S / G;                 // words per unit
   static constexpr int UV = S == 64 ? 1 : 32 / G;  // codes per unit
@@ -1355,9 +1363,9 @@ struct tma_shape {
   static constexpr int V = VPT / UV;               // units per thread per tile
   static constexpr int GROUP = tma_group(UW) < V ? tma_group(UW) : V;  // units per load
   static constexpr int LW = UW * GROUP;            // words per load
-  static constexpr int TILE_WORDS = kThreads * V * UW;
+  static constexpr int TILE_WORDS = NT * V * UW;
   static constexpr int TILE_BYTES = TILE_WORDS * 4;  // per vector
-  static constexpr uint64_t TILE_VALUES = static_cast<uint64_t>(kThreads) * VPT;
+  static constexpr uint64_t TILE_VALUES = static_cast<uint64_t>(NT) * VPT;
   static constexpr int RING_BYTES = RING;
   static constexpr int STAGES_RAW = RING_BYTES / (2 * TILE_BYTES);
   static constexpr int STAGES = STAGES_RAW < 2 ? 2 : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
@@ -1397,8 +1405,15 @@ constexpr int tma_ring_of() {
                           !std::is_same_v<Acc, acc_f32> && !std::is_same_v<Acc, acc_f32c>);
 }
 
+// Threads per block of the bulk-copy kernel.
+template <class Codec, class Acc>
+constexpr int tma_threads() {
+  return kThreads;
+}
+
 template <class Codec, class Acc, bool Short = false>
-using tma_shape_of = tma_shape<Codec::kS, tma_ring_of<Codec, Acc, Short>()>;
+using tma_shape_of = tma_shape<Codec::kS, tma_ring_of<Codec, Acc, Short>(), tma_vpt(Codec::kS),
+                               tma_threads<Codec, Acc>()>;
 
 // Whether the codec's single-DOT ring is deeper than the batched one.
 template <class Codec, class Acc>
@@ -1464,11 +1479,12 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src,
 }
 
 template <class Codec, class Acc, bool Short = false>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(tma_shape_of<Codec, Acc, Short>::NT)
     dot_tma_kernel(const dot_params p) {
-  extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ double scratch[kScratchDoubles];
   using shape = tma_shape_of<Codec, Acc, Short>;
+  constexpr int NT = shape::NT;
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ double scratch[scratch_doubles<NT>];
   constexpr int UV = shape::UV;
   constexpr int V = shape::V;
   constexpr int GROUP = shape::GROUP;
@@ -1484,28 +1500,60 @@ __global__ void __launch_bounds__(kThreads)
   const uint64_t yo = p.y_first + batch * p.y_index_stride;
   unsigned char *ring = smem + Codec::kTableBytes;
 
+  // Tiles are dealt round-robin: block b takes tiles b, b + G, ... (G =
+  // gridDim.x).  Co-resident blocks do not stream at equal speed (the SM's
+  // warp scheduler favours some), so with equal static shares the last
+  // blocks of a launch finish several microseconds after the median one.
+  // For codecs whose DOT is exact (kExactLanes: every partial sum is exact,
+  // so the summation order cannot change the result) the last kClaimRounds
+  // rounds of tiles are instead claimed one at a time from a counter
+  // (p.claims) by whichever block is free, which evens the finish out and
+  // keeps the result bit-identical.  The block holding the last ticket
+  // resets the counter.
+  constexpr uint64_t kNoTile = ~0ull;
+  constexpr uint64_t kClaimRounds = 2;
+  constexpr bool kMayClaim = Codec::kExactLanes;
+  const uint64_t G = gridDim.x;
   const uint64_t tiles = p.vector_ok ? p.n / shape::TILE_VALUES : 0;
-  const uint64_t mine =
-      tiles > blockIdx.x ? (tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+  const bool claiming = kMayClaim && p.claims != nullptr && tiles / G > kClaimRounds;
+  const uint64_t fixed_rounds = claiming ? tiles / G - kClaimRounds : 0;
+  const uint64_t mine =  // statically dealt tiles of this block
+      claiming ? fixed_rounds
+               : (tiles > blockIdx.x ? (tiles - blockIdx.x + G - 1) / G : 0);
+  __shared__ uint64_t stage_tile[kMayClaim ? STAGES : 1];
 
-  auto issue = [&](uint64_t k, uint32_t stage) {  // stage == k % STAGES
-    const uint64_t t = blockIdx.x + k * gridDim.x;
+  // Tile of the block's k-th stage fill (thread 0 only, in increasing k):
+  // dealt, claimed, or kNoTile once none is left (then every later k too).
+  auto tile_of = [&](uint64_t k) -> uint64_t {
+    if (k < mine) return blockIdx.x + k * G;
+    if (!claiming) return kNoTile;
+    const uint64_t t = fixed_rounds * G + atomicAdd(p.claims + batch, 1u);
+    return t < tiles ? t : kNoTile;
+  };
+  auto issue = [&](uint64_t t, uint32_t stage) {
     unsigned char *dst = ring + stage * (2 * TILE_BYTES);
     uint64_t *bar = &full[stage];
-    mbar_expect_tx(bar, 2u * TILE_BYTES);
-    if (t == p.stall_tile) return;  // failure-detection test: nothing lands
+    if constexpr (kMayClaim) stage_tile[stage] = t;  // ordered by the arrive below
+    mbar_expect_tx(bar, t == kNoTile ? 0u : 2u * TILE_BYTES);
+    if (t == kNoTile || t == p.stall_tile) return;  // stall: failure-detection test
     bulk_load(dst, xb + t * TILE_BYTES, TILE_BYTES, bar);
     bulk_load(dst + TILE_BYTES, yb + t * TILE_BYTES, TILE_BYTES, bar);
   };
+  // Fills k = 0 .. in flight after the loop stopped at k (claiming: every
+  // stage is refilled each round, with kNoTile at the end).
+  auto armed = [&](uint64_t j) { return claiming || j < mine; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1);
     mbar_fence_init();
   }
+  pdl_wait();
+  pdl_release();
   if constexpr (Codec::kTableBytes > 0) Codec::prepare(p, smem);
   __syncthreads();
   if (threadIdx.x == 0)
-    for (uint32_t k = 0; k < mine && k < static_cast<uint32_t>(STAGES); ++k) issue(k, k);
+    for (uint32_t k = 0; k < static_cast<uint32_t>(STAGES) && armed(k); ++k)
+      issue(tile_of(k), k);
 
   Acc acc;
   float lanes[4] = {0.f, 0.f, 0.f, 0.f};
@@ -1514,13 +1562,15 @@ __global__ void __launch_bounds__(kThreads)
   int since_flush = 0;
   uint32_t stage = 0, phase = 0;  // k % STAGES and (k / STAGES) & 1
   uint64_t k = 0;
-  for (; k < mine; ++k) {
+  for (; claiming || k < mine; ++k) {
     const bool ok = mbar_wait(&full[stage], phase, p.wait_cycles);
+    if constexpr (kMayClaim)
+      if (claiming && stage_tile[stage] == kNoTile) break;  // the same for all threads
     const uint32_t *xs = reinterpret_cast<const uint32_t *>(ring + stage * (2 * TILE_BYTES));
     const uint32_t *ys = xs + shape::TILE_WORDS;
 #pragma unroll
     for (int v = 0; v < V / GROUP; ++v) {
-      const int u = threadIdx.x + v * kThreads;  // load index
+      const int u = threadIdx.x + v * NT;  // load index
       uint32_t xw[LW], yw[LW];
       if constexpr (LW % 4 == 0) {
 #pragma unroll
@@ -1557,9 +1607,9 @@ __global__ void __launch_bounds__(kThreads)
       failed = true;
       break;
     }
-    if (threadIdx.x == 0 && k + STAGES < mine) {
+    if (threadIdx.x == 0 && (claiming || k + STAGES < mine)) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      issue(k + STAGES, stage);
+      issue(tile_of(k + STAGES), stage);
     }
     if (++stage == static_cast<uint32_t>(STAGES)) {
       stage = 0;
@@ -1570,7 +1620,7 @@ __global__ void __launch_bounds__(kThreads)
   if (failed) {
     // Let the copies this block still has in flight land before it exits.
     if (threadIdx.x == 0) {
-      for (uint64_t j = k; j < mine && j < k + STAGES; ++j)
+      for (uint64_t j = k; armed(j) && j < k + STAGES; ++j)
         mbar_wait(&full[j % STAGES], static_cast<uint32_t>((j / STAGES) & 1),
                   p.wait_cycles);
       atomicOr(p.status, static_cast<unsigned int>(AUT_STATUS_WAIT_TIMEOUT));
@@ -1580,9 +1630,10 @@ __global__ void __launch_bounds__(kThreads)
     ragged_tail<Codec>(xb, xo, yb, yo, tiles * shape::TILE_VALUES, p.n, acc, smem);
   }
   const dd mine_sum = failed ? dd{__longlong_as_double(0x7ff8000000000000ll), 0.0} : acc.pair();
-  const dd s = block_sum_dd(mine_sum, scratch);
-  grid_finish_dd(s, p.partials + 2 * static_cast<uint64_t>(batch) * gridDim.x,
-              p.tickets + batch, p.results + batch, scratch);
+  const dd s = block_sum_dd<NT>(mine_sum, scratch);
+  grid_finish_dd<NT>(s, p.partials + 2 * static_cast<uint64_t>(batch) * gridDim.x,
+                     p.tickets + batch, p.results + batch, scratch,
+                     claiming ? p.claims + batch : nullptr);
 }
 
 
@@ -1903,6 +1954,7 @@ struct kernel_entry {
   int runtime = 0;      // rt_codec: dot_params::rt carries the format
   kernel_fn batch_fn = nullptr;  // TMA: the short-ring kernel for batches
   int batch_smem = 0;
+  int threads = aut::dev::kThreads;  // per block
 };
 
 template <class Codec, class Acc>
@@ -1911,6 +1963,7 @@ void set_tma_kernels(kernel_entry &e) {
   e.fn = aut::dev::dot_tma_kernel<Codec, Acc>;
   e.smem = Codec::kTableBytes + shape::STAGES * 2 * shape::TILE_BYTES;
   e.tile_values = shape::TILE_VALUES;
+  e.threads = shape::NT;
   if constexpr (aut::dev::has_short_ring<Codec, Acc>) {
     using batch_shape = aut::dev::tma_shape_of<Codec, Acc, true>;
     static_assert(batch_shape::TILE_VALUES == shape::TILE_VALUES, "same tiles");
@@ -2251,7 +2304,7 @@ aut_status blocks_per_sm(kernel_entry &e) {
                                       e.smem));
   int b = 0;
   AUT_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-      &b, reinterpret_cast<const void *>(e.fn), aut::dev::kThreads, e.smem));
+      &b, reinterpret_cast<const void *>(e.fn), e.threads, e.smem));
   if (b < 1) return fail(AUT_ERR_UNSUPPORTED, "kernel does not fit on an SM");
   if (c.count < 256) {
     c.fns[c.count] = e.fn;
@@ -2313,6 +2366,26 @@ static aut::dev::dot_params params_for(const void *x, const void *y, uint64_t n,
   p.wait_cycles = aut::kWaitCyclesDefault;
   p.stall_tile = ~0ull;
   return p;
+}
+
+// Launches a DOT kernel with programmatic stream serialisation: it may be
+// scheduled while the kernel before it on the stream finishes (the kernels
+// call pdl_wait before their first global access, so they still see all
+// of that kernel's writes), which hides the launch gap between consecutive
+// DOTs.
+static cudaError_t launch_dependent(const kernel_entry &e, dim3 grid, cudaStream_t stream,
+                                    const aut::dev::dot_params &p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(static_cast<unsigned>(e.threads));
+  cfg.dynamicSmemBytes = static_cast<size_t>(e.smem);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, e.fn, p);
 }
 
 aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
@@ -2407,9 +2480,9 @@ aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
     p.status = status;
     p.wait_cycles = ws->wait_cycles;
     p.stall_tile = ws->stall_tile;
+    p.claims = ws->claims;
     dim3 grid(static_cast<unsigned>(per_pair), nb);
-    e.fn<<<grid, aut::dev::kThreads, e.smem, static_cast<cudaStream_t>(stream)>>>(p);
-    AUT_CUDA_TRY(cudaGetLastError());
+    AUT_CUDA_TRY(launch_dependent(e, grid, static_cast<cudaStream_t>(stream), p));
   }
   return AUT_OK;
 }
@@ -2582,7 +2655,7 @@ aut_status dot_launch_scratch(int sm_count, int32_t format, int32_t layout,
   if (clear_bytes > 0)
     AUT_CUDA_TRY(cudaMemsetAsync(clear, 0, clear_bytes, static_cast<cudaStream_t>(stream)));
   dim3 grid(static_cast<unsigned>(per_pair), batch);
-  e.fn<<<grid, aut::dev::kThreads, e.smem, static_cast<cudaStream_t>(stream)>>>(p);
+  e.fn<<<grid, e.threads, e.smem, static_cast<cudaStream_t>(stream)>>>(p);
   AUT_CUDA_TRY(cudaGetLastError());
   return AUT_OK;
 }

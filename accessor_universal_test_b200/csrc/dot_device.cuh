@@ -257,11 +257,16 @@ __device__ __forceinline__ dd warp_sum_dd(dd v) {
   return v;  // valid in lane 0
 }
 
-// Words of shared scratch the block reduction needs.
-constexpr int kScratchDoubles = 2 * (kThreads / 32);
+// Largest block of any DOT kernel, and the words of shared scratch the
+// block reduction needs for a block of NT threads.
+constexpr int kMaxThreads = 1024;
+template <int NT> constexpr int scratch_doubles = 2 * (NT / 32);
+constexpr int kScratchDoubles = scratch_doubles<kThreads>;
 
-// Sum over the block; the result is valid in thread 0.
+// Sum over a block of NT threads; the result is valid in thread 0.
+template <int NT = kThreads>
 __device__ __forceinline__ dd block_sum_dd(dd v, double *scratch) {
+  static_assert(NT % 32 == 0 && NT <= kMaxThreads, "whole warps, at most kMaxThreads");
   v = warp_sum_dd(v);
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -272,39 +277,66 @@ __device__ __forceinline__ dd block_sum_dd(dd v, double *scratch) {
   __syncthreads();
   dd s = {0.0, 0.0};
   if (warp == 0) {
-    if (lane < kThreads / 32) s = {scratch[2 * lane], scratch[2 * lane + 1]};
+    if (lane < NT / 32) s = {scratch[2 * lane], scratch[2 * lane + 1]};
     s = warp_sum_dd(s);
   }
   __syncthreads();
   return s;
 }
 
+// Programmatic dependent launch (the DOT kernels are launched with
+// programmatic stream serialisation, so a DOT may be scheduled while the
+// kernel before it on the stream is still finishing).  `pdl_wait` returns
+// once every grid this one depends on has completed and its memory is
+// visible: each DOT kernel calls it before its first global memory access,
+// so it reads its inputs, tables, partials and ticket exactly as with
+// ordinary stream order.  `pdl_release` then lets the next kernel on the
+// stream be scheduled: it takes effect once every block of this grid has
+// called it (so every block of this grid is resident by then) and the next
+// kernel still waits for this grid's completion before its own first
+// access.  Without the launch attribute both are no-ops.
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_release() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Single-pass grid reduction: every block publishes its partial (hi, lo at
-// partials[2b], [2b + 1]), the last block to arrive (atomic ticket after a
-// fence) sums the partials in block order and resets the ticket for the next
-// launch.  No block waits on another, so the pattern cannot hang.  The
-// result is hi + lo rounded once.
+// partials[2b], [2b + 1]) and takes a ticket with a release-acquire atomic
+// add, which orders the partial before the ticket; the last block to arrive
+// (its acquire, then the block barrier, orders every other block's partial
+// before its reads) sums the partials in block order and resets the ticket
+// for the next launch.  No block waits on another, so the pattern cannot
+// hang.  The result is hi + lo rounded once.  `claims` (optional) is a
+// counter every block has finished with by the time it takes its ticket; the
+// last block resets it too.
+template <int NT = kThreads>
 __device__ __forceinline__ void grid_finish_dd(dd block_partial, double *partials,
                                                unsigned int *ticket, double *result,
-                                               double *scratch) {
+                                               double *scratch,
+                                               unsigned int *claims = nullptr) {
   __shared__ bool last_block;
   if (threadIdx.x == 0) {
     partials[2 * blockIdx.x] = block_partial.hi;
     partials[2 * blockIdx.x + 1] = block_partial.lo;
-    __threadfence();
-    const unsigned int arrived = atomicAdd(ticket, 1u);
+    unsigned int arrived;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                 : "=r"(arrived)
+                 : "l"(ticket)
+                 : "memory");
     last_block = (arrived == gridDim.x - 1);
   }
   __syncthreads();
   if (!last_block) return;
-  __threadfence();
   dd s = {0.0, 0.0};
-  for (unsigned int b = threadIdx.x; b < gridDim.x; b += kThreads)
+  for (unsigned int b = threadIdx.x; b < gridDim.x; b += NT)
     s = dd_add(s, {__ldcg(partials + 2 * b), __ldcg(partials + 2 * b + 1)});
-  s = block_sum_dd(s, scratch);
+  s = block_sum_dd<NT>(s, scratch);
   if (threadIdx.x == 0) {
     *result = __dadd_rn(s.hi, s.lo);
     *ticket = 0u;
+    if (claims != nullptr) *claims = 0u;
   }
 }
 

@@ -96,8 +96,10 @@ struct aut_workspace {
   int sm_count = 0;
   int max_blocks = 0;       // per launch, all batches together
   double *partials = nullptr; // [kMaxBatchPerLaunch * max_blocks]
-  unsigned int *tickets = nullptr; // [kMaxBatchPerLaunch + 1], kept at zero;
-                                   // the last word is the sticky status
+  unsigned int *tickets = nullptr; // [2 * kMaxBatchPerLaunch + 1], kept at zero:
+                                   // the grid tickets, the sticky status word,
+                                   // then the dynamic-tail tile counters
+  unsigned int *claims = nullptr;  // = tickets + kMaxBatchPerLaunch + 1
   std::mutex mutex;
   // failure-detection test hook (aut_workspace_inject_stall)
   long long wait_cycles = aut::kWaitCyclesDefault;

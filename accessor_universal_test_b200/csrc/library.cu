@@ -108,6 +108,11 @@ aut_status fail(aut_status code, const std::string &message) {
 aut_status cuda_fail(cudaError_t err, const char *what) {
   last_error = std::string(what) + ": " + cudaGetErrorName(err) + " (" +
                cudaGetErrorString(err) + ")";
+  // The error is reported through the returned status; take it out of the
+  // runtime's per-thread last-error slot too, so that the caller's next
+  // cudaGetLastError (a framework checking its own launches) does not see
+  // it.  A sticky error (a lost context) stays whatever is done here.
+  (void)cudaGetLastError();
   return AUT_ERR_CUDA;
 }
 
@@ -530,10 +535,11 @@ aut_status aut_workspace_create(int32_t device, aut_workspace **out) {
   ws->sm_count = prop.multiProcessorCount;
   ws->max_blocks = prop.multiProcessorCount * (prop.maxThreadsPerMultiProcessor / 256);
   const size_t np = static_cast<size_t>(kMaxBatchPerLaunch) * ws->max_blocks;
-  const size_t nt = static_cast<size_t>(kMaxBatchPerLaunch) + 1;
+  const size_t nt = 2 * static_cast<size_t>(kMaxBatchPerLaunch) + 1;
   cudaError_t e = cudaMalloc(&ws->partials, np * sizeof(double));
   if (e == cudaSuccess) e = cudaMalloc(&ws->tickets, nt * sizeof(unsigned int));
   if (e == cudaSuccess) e = cudaMemset(ws->tickets, 0, nt * sizeof(unsigned int));
+  if (e == cudaSuccess) ws->claims = ws->tickets + kMaxBatchPerLaunch + 1;
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
     cudaFree(ws->partials);
