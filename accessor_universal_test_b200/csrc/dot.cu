@@ -1397,18 +1397,46 @@ constexpr int tma_ring(int s, bool fp64) {
 // run a second instantiation with the 64 KiB ring (`Short`). The ring depth
 // stays a compile-time constant: read from the launch parameters instead,
 // it cost the 10-bit codes 14 % (6337 -> 5475 GB/s).
+// Threads per block of the bulk-copy kernel.  Co-resident blocks of one
+// kernel do not stream at equal speed, so fewer, larger blocks per SM finish
+// closer together; whether that beats the extra warps of more blocks
+// depends on the decode.  From sweeps of 256/512/1024 threads on B200 (N =
+// 2^27, GB/s at 256 -> chosen): e2m3 dense 5548 -> 5622 (512), padded 4625
+// -> 4685 (512); e8m1 FP32 5915 -> 6295 (512); bf16 FP32 / FP64 6702 / 6411
+// -> 6809 / 6654 (512); padded E8 codes e8m0 3747 -> 3822, e8m3 FP64 4821
+// -> 4974 (512); raw FP32 6795 -> 7050 (512); e8m3 FP64 6129 -> 6324
+// (1024); e8m15 6711 -> 6889 (1024).  The others keep 256 (e8m0 and e8m1
+// FP64 lose 1-12 % at 512).
+template <class Codec> struct e8_shape {
+  static constexpr int S = 0, W = 0;
+};
+template <int S_, int W_> struct e8_shape<e8_codec<S_, W_>> {
+  static constexpr int S = S_, W = W_;
+};
+template <class Codec, class Acc>
+constexpr int tma_threads() {
+  constexpr int S = e8_shape<Codec>::S, W = e8_shape<Codec>::W;
+  constexpr bool f32 = std::is_same_v<Acc, acc_f32>;
+  if constexpr (std::is_same_v<Codec, e2m3_codec<6>> || std::is_same_v<Codec, e2m3_codec<8>>)
+    return 512;
+  else if constexpr ((S == 24 && W == 24) || (S == 12 && W == 12 && !f32))
+    return 1024;
+  else if constexpr ((S == 10 && W == 10 && f32) || S == 16 || S == 32)
+    return 512;
+  else
+    return kThreads;
+}
+
 template <class Codec, class Acc, bool Short>
 constexpr int tma_ring_of() {
   if (Codec::kTableBytes > 1024) return 32 * 1024;
-  return Short ? 64 * 1024
-               : tma_ring(Codec::kS,
-                          !std::is_same_v<Acc, acc_f32> && !std::is_same_v<Acc, acc_f32c>);
-}
-
-// Threads per block of the bulk-copy kernel.
-template <class Codec, class Acc>
-constexpr int tma_threads() {
-  return kThreads;
+  const int base = Short ? 64 * 1024
+                         : tma_ring(Codec::kS, !std::is_same_v<Acc, acc_f32> &&
+                                                   !std::is_same_v<Acc, acc_f32c>);
+  // blocks of 512 or 1024 threads take twice the ring of their 256-thread
+  // configuration, within 192 KiB
+  const int ring = tma_threads<Codec, Acc>() > kThreads ? 2 * base : base;
+  return ring > 192 * 1024 ? 192 * 1024 : ring;
 }
 
 template <class Codec, class Acc, bool Short = false>
@@ -2122,8 +2150,6 @@ kernel_entry wide_pick(int strategy, int accum) {
 int auto_strategy(int32_t format, int32_t layout, int32_t accum) {
   (void)layout;
   switch (format) {
-  case AUT_FMT_FP32:
-  case AUT_FMT_BF16_E8M7: return AUT_STRATEGY_LDG;
   case AUT_FMT_LNS8_R3:
   case AUT_FMT_LNS16_R11:
     return accum == AUT_ACCUM_FP32 ? AUT_STRATEGY_TMA : AUT_STRATEGY_LDG;
