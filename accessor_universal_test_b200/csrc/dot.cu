@@ -1439,9 +1439,15 @@ constexpr int tma_ring_of() {
   return ring > 192 * 1024 ? 192 * 1024 : ring;
 }
 
+// Codes per thread per tile of the bulk-copy kernel.
+template <class Codec, class Acc>
+constexpr int tma_vpt_of() {
+  return tma_vpt(Codec::kS);
+}
+
 template <class Codec, class Acc, bool Short = false>
-using tma_shape_of = tma_shape<Codec::kS, tma_ring_of<Codec, Acc, Short>(), tma_vpt(Codec::kS),
-                               tma_threads<Codec, Acc>()>;
+using tma_shape_of = tma_shape<Codec::kS, tma_ring_of<Codec, Acc, Short>(),
+                               tma_vpt_of<Codec, Acc>(), tma_threads<Codec, Acc>()>;
 
 // Whether the codec's single-DOT ring is deeper than the batched one.
 template <class Codec, class Acc>
