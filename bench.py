@@ -25,9 +25,11 @@ per_config  (one GPU) every other storage format of the benchmark's
             configurations at its stated size -- raw FP32/FP64 (with the
             N = 2^10 ... 2^27 sweep), e2m3 dense and padded, the E8 sweep with
             the FP64 accumulator, lns8_r3 / lns16_r11 on the cancellation
-            pair -- each accumulator and decoder: CUDA-event GB/s, fraction of
-            the measured peak, and the normalised error against the
-            reference's compensated long-double CPU DOT.
+            pair -- each accumulator and decoder: CUDA-event GB/s of packed
+            bits (the reference's metric: 2 N bits / 8), GB/s of the bytes the
+            layout moves (padded: whole 8/16/32-bit containers) and its
+            fraction of the measured peak, and the normalised error against
+            the reference's compensated long-double CPU DOT.
 
 The gemv workload runs aut_gemv instead: a 1024-row matrix of the E8 sweep
 formats with N / 1024 columns per GPU (rows sharded over GPUs, no
@@ -398,7 +400,8 @@ def run_per_config(ws, stream, threads, peak, reuse_refs):
         else:
             d, s, _ = cpu_reference_dot(name, stride, x.cpu().numpy().view(np.uint32),
                                         y.cpu().numpy().view(np.uint32), n, threads)
-        packed = 2 * n * bits / 8
+        packed = 2 * n * bits / 8   # the reference's GB/s counts packed bits
+        moved = 2 * n * stride / 8  # padded layouts move whole containers
         for acc in accums:
             acc_id = _lib.ACC_FP32 if acc == "fp32" else _lib.ACC_FP64
             for dec in decoders:
@@ -413,7 +416,8 @@ def run_per_config(ws, stream, threads, peak, reuse_refs):
                 e = {"group": group, "format": name, "layout": "dense" if layout == DENSE
                      else "padded", "accumulator": acc, "decoder": dec, "n": n, "ms": t_ms,
                      "gbs": packed / (t_ms / 1e3) / 1e9,
-                     "frac_of_peak": packed / (t_ms / 1e3) / 1e9 / peak,
+                     "gbs_moved": moved / (t_ms / 1e3) / 1e9,
+                     "frac_of_peak": moved / (t_ms / 1e3) / 1e9 / peak,
                      "normalized_error": normalized_error(got, d, s)}
                 if group == "lns":
                     e["condition_number"] = condition_number(d, s)
