@@ -1757,6 +1757,8 @@ __device__ __forceinline__ void gemv_publish(const gemv_params &g, uint32_t r, d
 __global__ void __launch_bounds__(kThreads)
     gemv_rows_kernel(const double *partials, uint32_t segments, uint32_t rows,
                      double *results) {
+  pdl_wait();  // the streaming kernel's partials
+  pdl_release();
   const uint32_t r = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
   const uint32_t lane = threadIdx.x & 31;
   if (r >= rows) return;
@@ -1806,6 +1808,8 @@ __global__ void __launch_bounds__(kThreads, Codec::kS == 12 ? 3 : 1)
     for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1);
     mbar_fence_init();
   }
+  pdl_wait();
+  pdl_release();
   if constexpr (Codec::kTableBytes > 0) Codec::prepare(dot_params{}, smem);
   __syncthreads();
   if (threadIdx.x == 0)
@@ -2411,19 +2415,26 @@ static aut::dev::dot_params params_for(const void *x, const void *y, uint64_t n,
 // call pdl_wait before their first global access, so they still see all
 // of that kernel's writes), which hides the launch gap between consecutive
 // DOTs.
-static cudaError_t launch_dependent(const kernel_entry &e, dim3 grid, cudaStream_t stream,
-                                    const aut::dev::dot_params &p) {
+template <class... P, class... A>
+static cudaError_t launch_pdl(void (*fn)(P...), dim3 grid, unsigned threads, size_t smem,
+                              cudaStream_t stream, A... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
-  cfg.blockDim = dim3(static_cast<unsigned>(e.threads));
-  cfg.dynamicSmemBytes = static_cast<size_t>(e.smem);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, e.fn, p);
+  return cudaLaunchKernelEx(&cfg, fn, args...);
+}
+
+static cudaError_t launch_dependent(const kernel_entry &e, dim3 grid, cudaStream_t stream,
+                                    const aut::dev::dot_params &p) {
+  return launch_pdl(e.fn, grid, static_cast<unsigned>(e.threads),
+                    static_cast<size_t>(e.smem), stream, p);
 }
 
 aut_status dot_launch(aut_workspace *ws, int32_t format, int32_t layout,
@@ -2636,13 +2647,14 @@ aut_status gemv_launch(aut_workspace *ws, int32_t format, int32_t layout, int32_
     g.partials = ws->partials;
     g.status = ws->tickets + kMaxBatchPerLaunch;
     dim3 grid(static_cast<unsigned>(segments), static_cast<unsigned>(blocks_y));
-    e.fn<<<grid, aut::dev::kThreads, e.smem, static_cast<cudaStream_t>(stream)>>>(g);
-    AUT_CUDA_TRY(cudaGetLastError());
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    AUT_CUDA_TRY(launch_pdl(e.fn, grid, aut::dev::kThreads, static_cast<size_t>(e.smem), s, g));
     constexpr uint64_t rows_per_block = aut::dev::kThreads / 32;
-    aut::dev::gemv_rows_kernel<<<static_cast<unsigned>((rc + rows_per_block - 1) / rows_per_block),
-                                 aut::dev::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-        ws->partials, static_cast<uint32_t>(segments), static_cast<uint32_t>(rc), results + r0);
-    AUT_CUDA_TRY(cudaGetLastError());
+    AUT_CUDA_TRY(launch_pdl(aut::dev::gemv_rows_kernel,
+                            dim3(static_cast<unsigned>((rc + rows_per_block - 1) / rows_per_block)),
+                            aut::dev::kThreads, 0, s, static_cast<const double *>(ws->partials),
+                            static_cast<uint32_t>(segments), static_cast<uint32_t>(rc),
+                            results + r0));
   }
   *handled = true;
   return AUT_OK;
