@@ -373,9 +373,18 @@ def run_per_config(ws, stream, threads, peak, reuse_refs):
     from accessor_universal_test_b200 import _lib, vectors
 
     def timed(fn, reps):
+        """Mean launch time over back-to-back launches; at least `reps`
+        launches and at least ~10 ms of device time, so that short DOTs are
+        not timed over a few hundred microseconds."""
         fn()
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(3):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        reps = max(reps, min(1000, int(10.0 / max(a.elapsed_time(b) / 3, 1e-3))))
         a.record()
         for _ in range(reps):
             fn()
