@@ -1771,9 +1771,18 @@ __global__ void __launch_bounds__(kThreads)
 
 // Three blocks per SM for the 12-bit codes (e8m3 4895 -> 5228 GB/s); the
 // 9-bit kernel's register-resident 64-value vector spills under that bound
-// (4330 -> 3873), the other widths do not change.
-template <class Codec>
-__global__ void __launch_bounds__(kThreads, Codec::kS == 12 ? 3 : 1)
+// (4330 -> 3873), the other widths do not change.  The FP64 rows take the
+// bound too: unbounded, the compiler spends 200-255 registers on them.
+//
+// F64 (E8 codes of at most 16 bits, FP64 accumulator): the product of a
+// matrix code and a vector value -- two bf16 values -- is exact in FP32
+// unless it falls below 2^-126 or overflows, so each product is widened to
+// FP64 once and summed in FP64 (as the DOT's e8_codec does); a chunk of 16
+// values whose smallest |product| is below 2^-126 (zeros included) or whose
+// sum is not finite is summed again from both operands widened, so every
+// row is an FP64 sum of exact products either way.
+template <class Codec, bool F64 = false>
+__global__ void __launch_bounds__(kThreads, Codec::kS == 12 || F64 ? 3 : 1)
     gemv_tma_kernel(const gemv_params g) {
   extern __shared__ __align__(128) unsigned char smem[];
   using shape = gemv_shape<Codec>;
@@ -1787,6 +1796,8 @@ __global__ void __launch_bounds__(kThreads, Codec::kS == 12 ? 3 : 1)
   constexpr int STAGES = shape::STAGES;
   constexpr int TILE_BYTES = shape::TILE_BYTES;
   static_assert(VPT <= 64, "two chains of at most 32 products per row tile");
+  static_assert(!F64 || (Codec::kW <= 16 && !is_e2m3<Codec>::value),
+                "FP64 rows for the bf16-exact E8 codes");
   __shared__ __align__(8) uint64_t full[STAGES];
   unsigned char *ring = smem + Codec::kTableBytes;
   constexpr int kRows = gemv_rows<Codec>();
@@ -1873,6 +1884,7 @@ __global__ void __launch_bounds__(kThreads, Codec::kS == 12 ? 3 : 1)
       ok = mbar_wait(&full[st], ph) && ok;
       const uint32_t *ws = reinterpret_cast<const uint32_t *>(ring + st * TILE_BYTES);
       float c0 = 0.f, c1 = 0.f;
+      double d0 = 0.0;  // F64
 #pragma unroll
       for (int v = 0; v < V / GROUP; ++v) {
         const int u = threadIdx.x + v * kThreads;
@@ -1892,6 +1904,40 @@ __global__ void __launch_bounds__(kThreads, Codec::kS == 12 ? 3 : 1)
         } else {
 #pragma unroll
           for (int q = 0; q < LW; ++q) w[q] = ws[u * LW + q];
+        }
+        if constexpr (F64) {
+          constexpr int C = UV * GROUP < 16 ? UV * GROUP : 16;  // values per check
+          static_assert((UV * GROUP) % C == 0, "whole chunks");
+#pragma unroll
+          for (int i0 = 0; i0 < UV * GROUP; i0 += C) {
+            double s0 = 0.0, s1 = 0.0;
+            float smallest = __int_as_float(0x7f800000);
+#pragma unroll
+            for (int i = i0; i < i0 + C; ++i) {
+              const int j = v * UV * GROUP + i;
+              const uint32_t m = field_top<S, W>(w, i);
+              const float pr = (j & 1) ? fma_bf16<true>(m, vec2[j >> 1], 0.f)
+                                       : fma_bf16<false>(m, vec2[j >> 1], 0.f);
+              smallest = fminf(smallest, fabsf(pr));
+              if (j & 1)
+                s1 += static_cast<double>(pr);
+              else
+                s0 += static_cast<double>(pr);
+            }
+            const double sc = s0 + s1;
+            if (smallest >= 1.17549435e-38f && fabs(sc) <= 1.7976931348623157e308) {
+              d0 += sc;
+            } else {
+#pragma unroll
+              for (int i = i0; i < i0 + C; ++i) {
+                const int j = v * UV * GROUP + i;
+                const uint32_t vb = (j & 1) ? (vec2[j >> 1] & 0xffff0000u) : (vec2[j >> 1] << 16);
+                d0 = fma(static_cast<double>(__uint_as_float(field_top<S, W>(w, i))),
+                         static_cast<double>(__uint_as_float(vb)), d0);
+              }
+            }
+          }
+          continue;
         }
         if constexpr (kE2m3) {
           // products of two f16 values into FP32, exactly (e2m3_codec::fma2):
@@ -1922,8 +1968,12 @@ __global__ void __launch_bounds__(kThreads, Codec::kS == 12 ? 3 : 1)
           }
         }
       }
-      red[(k + h) * kThreads + threadIdx.x] =
-          static_cast<double>(c0) + static_cast<double>(c1);
+      if constexpr (F64) {
+        red[(k + h) * kThreads + threadIdx.x] = d0;
+      } else {
+        red[(k + h) * kThreads + threadIdx.x] =
+            static_cast<double>(c0) + static_cast<double>(c1);
+      }
     }
     // every thread is done with these stages, and their rows of red are
     // complete, before the stages are refilled or the group reduced
@@ -2545,11 +2595,11 @@ struct gemv_entry {
   int group_rows = 0;
 };
 
-template <class Codec>
+template <class Codec, bool F64 = false>
 gemv_entry make_gemv_entry() {
   using shape = aut::dev::gemv_shape<Codec>;
   gemv_entry e;
-  e.fn = aut::dev::gemv_tma_kernel<Codec>;
+  e.fn = aut::dev::gemv_tma_kernel<Codec, F64>;
   e.smem = Codec::kTableBytes + shape::STAGES * shape::TILE_BYTES +
            aut::dev::gemv_rows<Codec>() * aut::dev::kThreads * 8;
   e.group_rows = aut::dev::gemv_rows<Codec>();
@@ -2558,9 +2608,26 @@ gemv_entry make_gemv_entry() {
   return e;
 }
 
-static gemv_entry gemv_lookup(int32_t format, int32_t layout) {
+// The vector-once kernels: FP32 rows of the E8 codes and raw FP32; FP64
+// rows of the E8 codes of at most 16 bits; e2m3 rows (exact) for both.
+static gemv_entry gemv_lookup(int32_t format, int32_t layout, int32_t accum) {
   using namespace aut::dev;
   const bool dense = layout == AUT_LAYOUT_DENSE;
+  if (accum == AUT_ACCUM_FP64) {
+    switch (format) {
+    case AUT_FMT_E8M0:
+      return dense ? make_gemv_entry<e8_codec<9, 9>, true>() : make_gemv_entry<e8_codec<16, 9>, true>();
+    case AUT_FMT_E8M1:
+      return dense ? make_gemv_entry<e8_codec<10, 10>, true>() : make_gemv_entry<e8_codec<16, 10>, true>();
+    case AUT_FMT_E8M3:
+      return dense ? make_gemv_entry<e8_codec<12, 12>, true>() : make_gemv_entry<e8_codec<16, 12>, true>();
+    case AUT_FMT_E8M5:
+      return dense ? make_gemv_entry<e8_codec<14, 14>, true>() : make_gemv_entry<e8_codec<16, 14>, true>();
+    case AUT_FMT_BF16_E8M7: return make_gemv_entry<e8_codec<16, 16>, true>();
+    case AUT_FMT_E2M3: break;
+    default: return {};
+    }
+  }
   switch (format) {
   case AUT_FMT_FP32: return make_gemv_entry<e8_codec<32, 32>>();
   case AUT_FMT_E8M0: return dense ? make_gemv_entry<e8_codec<9, 9>>() : make_gemv_entry<e8_codec<16, 9>>();
@@ -2611,11 +2678,10 @@ aut_status gemv_launch(aut_workspace *ws, int32_t format, int32_t layout, int32_
                        const void *vector, uint64_t rows, uint64_t columns,
                        double *results, void *stream, bool *handled) {
   *handled = false;
-  // e2m3 rows are exact up to their final rounding with either accumulator
-  if (accum != AUT_ACCUM_FP32 && format != AUT_FMT_E2M3) return AUT_OK;
+  if (accum != AUT_ACCUM_FP32 && accum != AUT_ACCUM_FP64) return AUT_OK;
   if (strategy != AUT_STRATEGY_AUTO && strategy != AUT_STRATEGY_TMA) return AUT_OK;
   if (decoder != AUT_DECODER_AUTO && decoder != AUT_DECODER_DIRECT) return AUT_OK;
-  const gemv_entry e = gemv_lookup(format, layout);
+  const gemv_entry e = gemv_lookup(format, layout, accum);
   if (e.fn == nullptr || columns == 0 || rows == 0 || columns % e.tile_values != 0) return AUT_OK;
   if ((reinterpret_cast<uintptr_t>(matrix) | reinterpret_cast<uintptr_t>(vector)) & 15u)
     return AUT_OK;

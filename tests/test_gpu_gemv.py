@@ -128,16 +128,61 @@ def test_gemv_degenerate_shapes(ws):
 VECTOR_ONCE = ["e8m0", "e8m1", "e8m3", "e8m5", "bf16_e8m7", "e8m15", "fp32", "e2m3"]
 
 
+# FP64 rows decode the vector once for the E8 codes of at most 16 bits
+VECTOR_ONCE_F64 = ["e8m0", "e8m1", "e8m3", "e8m5", "bf16_e8m7"]
+
+
 @pytest.mark.parametrize("name", VECTOR_ONCE)
 @pytest.mark.parametrize("layout", [0, 1])
-def test_gemv_vector_once_rows_match_oracle(ws, orc, name, layout):
+@pytest.mark.parametrize("accum", [0, 1])
+def test_gemv_vector_once_rows_match_oracle(ws, orc, name, layout, accum):
+    if accum == 1 and name not in VECTOR_ONCE_F64:
+        pytest.skip("FP64 rows of this format take the batch path")
     # 1 row; 37 rows (a ragged group of 5); 1030 rows (two launches)
     for rows, columns in ((1, 16384), (37, 32768), (1030, 16384)):
         if name == "fp32" and layout == 1:
             continue
         m, v, ref = _operands(ws, orc, name, layout, rows, columns)
-        got = _gemv(ws, name, layout, 0, m, v, rows, columns)
-        _check_rows(got, ref, 0, rows, (name, layout, rows, columns))
+        got = _gemv(ws, name, layout, accum, m, v, rows, columns)
+        _check_rows(got, ref, accum, rows, (name, layout, accum, rows, columns))
+
+
+@pytest.mark.parametrize("layout", [0, 1])
+def test_gemv_fp64_rows_with_tiny_and_huge_products(ws, orc, layout):
+    """FP64 rows of e8m5 whose products fall below 2^-126 or overflow FP32:
+    those row tiles are summed again from widened operands, so every row is
+    the FP64 sum of exact products (compared with the long-double oracle)."""
+    import torch
+    from accessor_universal_test_b200 import _lib
+    rows, columns = 12, 16384
+    desc = _lib.format_info(_lib.format_id("e8m5"))
+    vals = orc.synthetic(0, 11, 0, rows * columns).reshape(rows, columns)
+    vec = orc.synthetic(0, 11, 1, columns)
+    vals[2, 10:40] *= 2.0 ** -120      # times the vector values below: under 2^-126
+    vec[10:40] *= 2.0 ** -10
+    vals[6, 3000] = 2.0 ** 100         # times a vector value of 2^60: over FP32
+    vec[3000] = 2.0 ** 60
+    vals[9, :] = 0.0                   # a row of zero products
+    mc = orc.encode(desc, vals.ravel())
+    vc = orc.encode(desc, vec)
+    fid = _lib.format_id("e8m5")
+    bufs = []
+    for codes in (mc, vc):
+        if layout == 0:
+            words = orc.pack_dense(desc[1], codes)
+            data = words.view(np.uint8).copy()
+        else:
+            data = codes.astype(np.uint16).view(np.uint8).copy()
+        bufs.append(torch.from_numpy(data).cuda())
+    got = _gemv(ws, "e8m5", layout, 1, bufs[0], bufs[1], rows, columns)
+    for r in range(rows):
+        d, s = orc.dot_codes(desc, mc[r * columns:(r + 1) * columns], vc, threads=1)
+        want = np.longdouble(d[0]) + np.longdouble(d[1])
+        sabs = np.longdouble(s[0]) + np.longdouble(s[1])
+        if sabs == 0:
+            assert got[r] == 0.0, (r, got[r])
+        else:
+            assert normalized_error(got[r], want, sabs) <= TOL[1], (r, got[r], float(want))
 
 
 def test_gemv_vector_once_is_deterministic(ws, orc):
@@ -187,8 +232,9 @@ def test_gemv_vector_once_special_values(ws, orc):
 @pytest.mark.parametrize("name", ["e8m0", "e8m5", "e8m15"])
 def test_gemv_whole_segments_on_the_batch_path(ws, orc, name):
     """Whole-segment shapes that the vector-once kernel does not take: the
-    FP64 accumulator, the LDG strategy, and a matrix that does not start on
-    a 16-byte boundary (value-index rows on the per-value path)."""
+    FP64 accumulator for 24-bit codes, the LDG strategy, and a matrix that
+    does not start on a 16-byte boundary (value-index rows on the per-value
+    path)."""
     import torch
     from accessor_universal_test_b200 import _lib
     rows, columns = 19, 16384

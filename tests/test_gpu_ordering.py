@@ -101,3 +101,33 @@ def test_batched_exact_dots_claim_tiles_per_pair(ws):
                        res.data_ptr())
         torch.cuda.synchronize()
         assert res.cpu().numpy().tolist() == singles
+
+
+def test_dot_after_host_to_device_copies_on_one_stream(ws):
+    """The e2e pattern: pinned host buffers copied into the same device
+    buffers round after round, each round's DOT enqueued right after its
+    copies (copies are not kernels: the DOT waits for them in full)."""
+    import torch
+    from accessor_universal_test_b200 import _lib
+    name, layout, accum = "e8m3", 0, 0
+    fid = _lib.format_id(name)
+    n = (1 << 22) + 3
+    rounds = []
+    for r in range(3):
+        x, y = device_pair(ws, name, layout, n, seed=SEED + 5 * r)
+        rounds.append((x.cpu().pin_memory(), y.cpu().pin_memory(),
+                       gpu_dot(ws, name, layout, accum, x, y, n)))
+        del x, y
+    dx = torch.empty_like(rounds[0][0], device="cuda")
+    dy = torch.empty_like(rounds[0][1], device="cuda")
+    res = torch.full((len(rounds),), float("nan"), dtype=torch.float64, device="cuda")
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for r, (hx, hy, _) in enumerate(rounds):
+            dx.copy_(hx, non_blocking=True)
+            dy.copy_(hy, non_blocking=True)
+            ws.dot(fid, layout, accum, dx.data_ptr(), dy.data_ptr(), n,
+                   res.data_ptr() + 8 * r, stream.cuda_stream)
+    stream.synchronize()
+    assert res.cpu().numpy().tolist() == [expect for _, _, expect in rounds]
