@@ -29,7 +29,9 @@ per_config  (one GPU) every other storage format of the benchmark's
             bits (the reference's metric: 2 N bits / 8), GB/s of the bytes the
             layout moves (padded: whole 8/16/32-bit containers) and its
             fraction of the measured peak, and the normalised error against
-            the reference's compensated long-double CPU DOT.
+            the reference's compensated long-double CPU DOT.  Also the GEMV (1024 x 2^17,
+            vector in the same format) of the E8 sweep formats (FP32, FP64),
+            e2m3 (dense, padded) and lns8_r3, error over three sampled rows.
 
 The gemv workload runs aut_gemv instead: a 1024-row matrix of the E8 sweep
 formats with N / 1024 columns per GPU (rows sharded over GPUs, no
@@ -101,6 +103,11 @@ PER_CONFIG = [
      ("auto", "fraction_lut_fused", "fraction_lut", "full_lut", "ex2_approx")),
 ]
 RAW_SWEEP = [10, 16, 20, 23, 26, 27]
+# GEMV rows of per_config: (format, generator kind, layout, accumulators)
+GEMV_CONFIG = [(f, k, DENSE, ("fp32", "fp64")) for f, k in E8_SWEEP] + [
+    ("e2m3", 2, DENSE, ("fp32",)), ("e2m3", 2, PADDED, ("fp32",)),
+    ("lns8_r3", 3, DENSE, ("fp32", "fp64")),
+]
 
 
 def parse():
@@ -432,6 +439,49 @@ def run_per_config(ws, stream, threads, peak, reuse_refs):
                     e["condition_number"] = condition_number(d, s)
                 entries.append(e)
         del x, y
+        torch.cuda.empty_cache()
+    # GEMV over the same storage (1024 rows x 2^17 columns, the vector in the
+    # same format): packed bytes = (rows * columns + columns) * bits / 8; the
+    # error is the largest normalised error of three sampled rows
+    rows, cols = GEMV_ROWS, 1 << 17
+    for name, kind, layout, accs in GEMV_CONFIG:
+        fid = _lib.format_id(name)
+        ws.prepare(fid)
+        fam, bits, _, _ = _lib.format_info(fid)
+        m = vectors.encoded(ws, fid, layout, kind, SEED, 0, rows * cols)
+        v = vectors.encoded(ws, fid, layout, kind, SEED, 1, cols)
+        out = torch.zeros(rows, dtype=torch.float64, device="cuda")
+        torch.cuda.synchronize()
+        stride = bits if layout == DENSE else (8 if bits <= 8 else 16 if bits <= 16 else 32)
+        row_bytes = cols * stride // 8
+        mh = m.cpu().numpy()
+        vw = v.cpu().numpy().view(np.uint32)
+        refs = []
+        for r in (0, rows // 2, rows - 1):
+            seg = np.zeros(row_bytes + 16, dtype=np.uint8)
+            avail = mh[r * row_bytes: r * row_bytes + row_bytes + 16]
+            seg[:avail.size] = avail
+            refs.append((r, cpu_reference_dot(name, stride, seg.view(np.uint32), vw, cols,
+                                              threads)[:2]))
+        packed = (rows * cols + cols) * bits / 8
+        moved = (rows * cols + cols) * stride / 8
+        for acc in accs:
+            acc_id = _lib.ACC_FP32 if acc == "fp32" else _lib.ACC_FP64
+
+            def launch():
+                ws.gemv(fid, layout, acc_id, m.data_ptr(), v.data_ptr(), rows, cols,
+                        out.data_ptr(), stream)
+            t_ms = timed(launch, 20)
+            got = out.cpu().numpy()
+            err = max(normalized_error(got[r], d, s_) for r, (d, s_) in refs)
+            entries.append({"group": "gemv", "format": name, "layout": "dense" if layout == DENSE
+                            else "padded", "accumulator": acc, "decoder": "auto",
+                            "n": rows * cols, "rows": rows, "columns": cols, "ms": t_ms,
+                            "gbs": packed / (t_ms / 1e3) / 1e9,
+                            "gbs_moved": moved / (t_ms / 1e3) / 1e9,
+                            "frac_of_peak": moved / (t_ms / 1e3) / 1e9 / peak,
+                            "normalized_error": err})
+        del m, v, out
         torch.cuda.empty_cache()
     if ws.status() != 0:
         raise RuntimeError("a bounded device wait timed out during the configurations")
