@@ -325,6 +325,7 @@ template <typename T> struct lane_table {
 template <typename T> struct lns8_codec {
   using table = lane_table<T>;
   static constexpr int kS = 8;
+  static constexpr int kW = 8;
   static constexpr int kU = 4;
   static constexpr int kTableBytes = table::bytes(256);
   static constexpr bool kExactLanes = false;
@@ -1700,6 +1701,7 @@ struct gemv_params {
   uint32_t groups_per_block;   // groups of gemv_rows<Codec>() rows
   double *partials;            // [rows][gridDim.x]
   unsigned int *status;
+  const void *table;           // decode table (lns8_r3)
 };
 
 template <class Codec> struct is_e2m3 : std::false_type {};
@@ -1821,7 +1823,11 @@ __global__ void __launch_bounds__(kThreads, Codec::kS == 12 || F64 ? 3 : 1)
   }
   pdl_wait();
   pdl_release();
-  if constexpr (Codec::kTableBytes > 0) Codec::prepare(dot_params{}, smem);
+  if constexpr (Codec::kTableBytes > 0) {
+    dot_params tp{};
+    tp.table = g.table;
+    Codec::prepare(tp, smem);
+  }
   __syncthreads();
   if (threadIdx.x == 0)
     for (uint32_t t = 0; t < tiles && t < static_cast<uint32_t>(STAGES); ++t) issue(t, t);
@@ -1829,8 +1835,10 @@ __global__ void __launch_bounds__(kThreads, Codec::kS == 12 || F64 ? 3 : 1)
   // this thread's codes of the vector segment, decoded once: codes of up to
   // 16 bits are bf16 values exactly and are kept as bf16 pairs (half the
   // registers, so more blocks fit an SM); wider ones as FP32; e2m3 codes as
-  // the f16 pairs of the hardware conversion
-  constexpr bool kPairs = W <= 16;
+  // the f16 pairs of the hardware conversion; lns8_r3 codes as the FP32
+  // values of their per-lane table
+  constexpr bool kLns = std::is_same_v<Codec, lns8_codec<float>>;
+  constexpr bool kPairs = W <= 16 && !kLns;
   float vec[kPairs ? 1 : VPT];
   uint32_t vec2[kPairs ? VPT / 2 : 1];
   {
@@ -1848,6 +1856,14 @@ __global__ void __launch_bounds__(kThreads, Codec::kS == 12 || F64 ? 3 : 1)
           const int j = (v * UV * GROUP) / 2 + 2 * q;  // f16 pair index
           Codec::to_f16x2x2(Codec::bytes4(w, q, smem), vec2[j], vec2[j + 1]);
         }
+        continue;
+      }
+      if constexpr (kLns) {
+        const uint32_t lane_off = Codec::table::lane_offset();
+#pragma unroll
+        for (int i = 0; i < UV * GROUP; ++i)
+          vec[v * UV * GROUP + i] =
+              Codec::table::at(smem, __byte_perm(w[i >> 2], 0u, 0x4440u + (i & 3)), lane_off);
         continue;
       }
 #pragma unroll
@@ -1904,6 +1920,20 @@ __global__ void __launch_bounds__(kThreads, Codec::kS == 12 || F64 ? 3 : 1)
         } else {
 #pragma unroll
           for (int q = 0; q < LW; ++q) w[q] = ws[u * LW + q];
+        }
+        if constexpr (kLns) {
+          const uint32_t lane_off = Codec::table::lane_offset();
+#pragma unroll
+          for (int i = 0; i < UV * GROUP; ++i) {
+            const int j = v * UV * GROUP + i;
+            const float mv =
+                Codec::table::at(smem, __byte_perm(w[i >> 2], 0u, 0x4440u + (i & 3)), lane_off);
+            if (i & 1)
+              c1 = fmaf(mv, vec[j], c1);
+            else
+              c0 = fmaf(mv, vec[j], c0);
+          }
+          continue;
         }
         if constexpr (F64) {
           constexpr int C = UV * GROUP < 16 ? UV * GROUP : 16;  // values per check
@@ -2608,8 +2638,9 @@ gemv_entry make_gemv_entry() {
   return e;
 }
 
-// The vector-once kernels: FP32 rows of the E8 codes and raw FP32; FP64
-// rows of the E8 codes of at most 16 bits; e2m3 rows (exact) for both.
+// The vector-once kernels: FP32 rows of the E8 codes, raw FP32 and
+// lns8_r3 (its per-lane table); FP64 rows of the E8 codes of at most 16
+// bits; e2m3 rows (exact) for both.
 static gemv_entry gemv_lookup(int32_t format, int32_t layout, int32_t accum) {
   using namespace aut::dev;
   const bool dense = layout == AUT_LAYOUT_DENSE;
@@ -2637,6 +2668,7 @@ static gemv_entry gemv_lookup(int32_t format, int32_t layout, int32_t accum) {
   case AUT_FMT_BF16_E8M7: return make_gemv_entry<e8_codec<16, 16>>();
   case AUT_FMT_E8M15: return dense ? make_gemv_entry<e8_codec<24, 24>>() : make_gemv_entry<e8_codec<32, 24>>();
   case AUT_FMT_E2M3: return dense ? make_gemv_entry<e2m3_codec<6>>() : make_gemv_entry<e2m3_codec<8>>();
+  case AUT_FMT_LNS8_R3: return make_gemv_entry<lns8_codec<float>>();  // one code per byte
   default: return {};
   }
 }
@@ -2690,6 +2722,13 @@ aut_status gemv_launch(aut_workspace *ws, int32_t format, int32_t layout, int32_
   int per_sm = 0;
   aut_status st = gemv_blocks_per_sm(e, &per_sm);
   if (st != AUT_OK) return st;
+  const void *table = nullptr;
+  if (format == AUT_FMT_LNS8_R3) {
+    const code_tables *t = nullptr;
+    st = code_tables_for(ws, format, &t);
+    if (st != AUT_OK) return st;
+    table = t->full_f32;
+  }
   const uint64_t row_bytes = segments * e.tile_bytes;
   const uint64_t cap = static_cast<uint64_t>(ws->sm_count) * per_sm;
   const uint64_t group_rows = static_cast<uint64_t>(e.group_rows);
@@ -2712,6 +2751,7 @@ aut_status gemv_launch(aut_workspace *ws, int32_t format, int32_t layout, int32_
     g.groups_per_block = static_cast<uint32_t>(groups_per_block);
     g.partials = ws->partials;
     g.status = ws->tickets + kMaxBatchPerLaunch;
+    g.table = table;
     dim3 grid(static_cast<unsigned>(segments), static_cast<unsigned>(blocks_y));
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     AUT_CUDA_TRY(launch_pdl(e.fn, grid, aut::dev::kThreads, static_cast<size_t>(e.smem), s, g));

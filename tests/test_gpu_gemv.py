@@ -122,10 +122,10 @@ def test_gemv_degenerate_shapes(ws):
     assert info.value.status == _lib.AUT_ERR_TOO_LARGE
 
 
-# The FP32 GEMV of the E8 codes and raw FP32 decodes the vector once per block
-# when the columns are whole segments (one bulk-copy tile per row: 16384
-# values for 9-bit codes, 8192 for the others).
-VECTOR_ONCE = ["e8m0", "e8m1", "e8m3", "e8m5", "bf16_e8m7", "e8m15", "fp32", "e2m3"]
+# The FP32 GEMV of the E8 codes, raw FP32 and lns8_r3 decodes the vector once
+# per block when the columns are whole segments (one bulk-copy tile per row:
+# 16384 values for 9- and 8-bit codes, 8192 for the others).
+VECTOR_ONCE = ["e8m0", "e8m1", "e8m3", "e8m5", "bf16_e8m7", "e8m15", "fp32", "e2m3", "lns8_r3"]
 
 
 # FP64 rows decode the vector once for the E8 codes of at most 16 bits
