@@ -1776,7 +1776,8 @@ __global__ void __launch_bounds__(kThreads)
 // (4330 -> 3873), the other widths do not change.  The FP64 rows take the
 // bound too: unbounded, the compiler spends 200-255 registers on them.
 //
-// F64 (E8 codes of at most 16 bits, FP64 accumulator): the product of a
+// F64 (FP64 accumulator): 24- and 32-bit codes multiply both operands
+// widened to FP64 (exact products).  For E8 codes of at most 16 bits the product of a
 // matrix code and a vector value -- two bf16 values -- is exact in FP32
 // unless it falls below 2^-126 or overflows, so each product is widened to
 // FP64 once and summed in FP64 (as the DOT's e8_codec does); a chunk of 16
@@ -1798,8 +1799,8 @@ __global__ void __launch_bounds__(kThreads, Codec::kS == 12 || F64 ? 3 : 1)
   constexpr int STAGES = shape::STAGES;
   constexpr int TILE_BYTES = shape::TILE_BYTES;
   static_assert(VPT <= 64, "two chains of at most 32 products per row tile");
-  static_assert(!F64 || (Codec::kW <= 16 && !is_e2m3<Codec>::value),
-                "FP64 rows for the bf16-exact E8 codes");
+  static_assert(!F64 || (!is_e2m3<Codec>::value && Codec::kTableBytes == 0),
+                "FP64 rows for the E8 codes and raw FP32");
   __shared__ __align__(8) uint64_t full[STAGES];
   unsigned char *ring = smem + Codec::kTableBytes;
   constexpr int kRows = gemv_rows<Codec>();
@@ -1932,6 +1933,16 @@ __global__ void __launch_bounds__(kThreads, Codec::kS == 12 || F64 ? 3 : 1)
               c1 = fmaf(mv, vec[j], c1);
             else
               c0 = fmaf(mv, vec[j], c0);
+          }
+          continue;
+        }
+        if constexpr (F64 && W > 16) {
+          // 24- and 32-bit codes: both operands widened, exact products
+#pragma unroll
+          for (int i = 0; i < UV * GROUP; ++i) {
+            const int j = v * UV * GROUP + i;
+            d0 = fma(static_cast<double>(__uint_as_float(field_top<S, W>(w, i))),
+                     static_cast<double>(vec[j]), d0);
           }
           continue;
         }
@@ -2639,8 +2650,8 @@ gemv_entry make_gemv_entry() {
 }
 
 // The vector-once kernels: FP32 rows of the E8 codes, raw FP32 and
-// lns8_r3 (its per-lane table); FP64 rows of the E8 codes of at most 16
-// bits; e2m3 rows (exact) for both.
+// lns8_r3 (its per-lane table); FP64 rows of the E8 codes and raw FP32;
+// e2m3 rows (exact) for both.
 static gemv_entry gemv_lookup(int32_t format, int32_t layout, int32_t accum) {
   using namespace aut::dev;
   const bool dense = layout == AUT_LAYOUT_DENSE;
@@ -2655,6 +2666,9 @@ static gemv_entry gemv_lookup(int32_t format, int32_t layout, int32_t accum) {
     case AUT_FMT_E8M5:
       return dense ? make_gemv_entry<e8_codec<14, 14>, true>() : make_gemv_entry<e8_codec<16, 14>, true>();
     case AUT_FMT_BF16_E8M7: return make_gemv_entry<e8_codec<16, 16>, true>();
+    case AUT_FMT_E8M15:
+      return dense ? make_gemv_entry<e8_codec<24, 24>, true>() : make_gemv_entry<e8_codec<32, 24>, true>();
+    case AUT_FMT_FP32: return make_gemv_entry<e8_codec<32, 32>, true>();
     case AUT_FMT_E2M3: break;
     default: return {};
     }

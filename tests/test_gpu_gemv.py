@@ -128,8 +128,8 @@ def test_gemv_degenerate_shapes(ws):
 VECTOR_ONCE = ["e8m0", "e8m1", "e8m3", "e8m5", "bf16_e8m7", "e8m15", "fp32", "e2m3", "lns8_r3"]
 
 
-# FP64 rows decode the vector once for the E8 codes of at most 16 bits
-VECTOR_ONCE_F64 = ["e8m0", "e8m1", "e8m3", "e8m5", "bf16_e8m7"]
+# FP64 rows decode the vector once for the E8 codes and raw FP32
+VECTOR_ONCE_F64 = ["e8m0", "e8m1", "e8m3", "e8m5", "bf16_e8m7", "e8m15", "fp32", "e2m3"]
 
 
 @pytest.mark.parametrize("name", VECTOR_ONCE)
@@ -232,9 +232,9 @@ def test_gemv_vector_once_special_values(ws, orc):
 @pytest.mark.parametrize("name", ["e8m0", "e8m5", "e8m15"])
 def test_gemv_whole_segments_on_the_batch_path(ws, orc, name):
     """Whole-segment shapes that the vector-once kernel does not take: the
-    FP64 accumulator for 24-bit codes, the LDG strategy, and a matrix that
-    does not start on a 16-byte boundary (value-index rows on the per-value
-    path)."""
+    LDG strategy and a matrix that does not start on a 16-byte boundary
+    (value-index rows on the per-value path); and the FP64 rows beside
+    them."""
     import torch
     from accessor_universal_test_b200 import _lib
     rows, columns = 19, 16384
