@@ -296,14 +296,15 @@ template <int S> struct e2m3_codec {
   }
 };
 
-// Copies of a small decode table in shared memory, one per lane, so a
-// warp's lookups never share a bank: entry e of copy c at element
-// e * kCopies + c.  (8-byte entries would be conflict-free with 16 copies,
-// a half warp per wavefront, but the extra blocks that the halved table
-// lets onto an SM then saturate the shared-memory pipe: lns8_r3 with the
-// FP64 accumulator, 3650 -> 3355 GB/s; 32 copies are kept.)
-template <typename T> struct lane_table {
-  static constexpr int kCopies = 32;
+// Copies of a small decode table in shared memory, one per lane (C = 32),
+// so a warp's lookups never share a bank: entry e of copy c at element
+// e * kCopies + c.  (8-byte entries are conflict-free with 16 copies, a
+// half warp per wavefront; for the full lns8_r3 table the extra blocks that
+// the halved table lets onto an SM then saturate the shared-memory pipe --
+// FP64, 3650 -> 3355 GB/s -- so it keeps 32, while the fused-sum table,
+// one lookup per pair, takes 16.)
+template <typename T, int C = 32> struct lane_table {
+  static constexpr int kCopies = C;
   static constexpr uint32_t kEntryBytes = kCopies * static_cast<uint32_t>(sizeof(T));
   static constexpr int bytes(int entries) { return entries * static_cast<int>(kEntryBytes); }
   __device__ __forceinline__ static uint32_t lane_offset() {
@@ -384,7 +385,10 @@ template <typename T> struct lns8_codec {
 // zeroes products with a zero operand, and a reserved code with its sign bit
 // set (NaN) raises a flag that makes the DOT NaN.
 template <typename T> struct lns8_fused_codec {
-  using table = lane_table<T>;
+  // FP64: 16 copies (a half warp per 8-byte wavefront is still conflict-free)
+  // halve the 64 KiB table, so more blocks fit (N = 2^28, GB/s thread
+  // packets / bulk copies: 3177 / 2412 -> 3320 / 3249)
+  using table = lane_table<T, sizeof(T) == 8 ? 16 : 32>;
   static constexpr int kS = 8;
   static constexpr int kU = 4;
   static constexpr int kEntry = static_cast<int>(sizeof(T));
