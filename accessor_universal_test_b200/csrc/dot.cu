@@ -372,54 +372,63 @@ template <typename T> struct lns8_codec {
 
 // lns8_r3 with the fused-sum decoder (fused_sum_lut_shared,
 // lns_decoder_strategies.cuh:327-347): the two log codes are added and one
-// lookup in a table of every product magnitude serves the pair.  Each 7-bit
+// lookup in a table of every signed product serves the pair.  Each 7-bit
 // log code is biased by 2^6 (reserved code -> 0, finite codes -> [1, 127]),
 // so one 32-bit add sums the four byte lanes of a word pair without a carry
-// crossing them, and byte k of the sum indexes the table directly (entry i
-// = T(exp2((i - 128) / 8)), the reference's product table shifted by two
-// slots).  The table is replicated per lane (entry i of lane l at i * 32 +
-// l), so the lookups of a warp never share a bank.  Reserved codes follow
+// crossing them: byte k of the sum is the biased product log h of pair k.
+// The table holds 512 signed products, entry s * 256 + h = (-1)^s *
+// T(exp2((h - 128) / 8)) (the reference's product table shifted by two
+// slots, and its negation), with entries 0 and 256 = +0; one byte permute
+// per pair builds the index from byte k of the sums and byte k of the
+// product signs (moved to bit 0 of each byte once per word).  The table is
+// replicated per lane (entry i of lane l at i * kCopies + l % kCopies), so
+// the lookups of a warp never share a bank.  Reserved codes follow
 // lns::multiply_codes (lns_benchmark_core.hpp:241-254) without branches:
 // adding 0x7f to a biased byte sets its top bit exactly when the code is not
-// reserved, a sign-replicating byte permute spreads that bit into a mask that
-// zeroes products with a zero operand, and a reserved code with its sign bit
-// set (NaN) raises a flag that makes the DOT NaN.
+// reserved, a sign-replicating byte permute spreads that bit over its byte,
+// and the sums are masked with it once per word, so a pair with a zero
+// operand reads entry 0 or 256; a reserved code with its sign bit set (NaN)
+// raises a flag that makes the DOT NaN.
 template <typename T> struct lns8_fused_codec {
   // FP64: 16 copies (a half warp per 8-byte wavefront is still conflict-free)
-  // halve the 64 KiB table, so more blocks fit (N = 2^28, GB/s thread
-  // packets / bulk copies: 3177 / 2412 -> 3320 / 3249)
   using table = lane_table<T, sizeof(T) == 8 ? 16 : 32>;
   static constexpr int kS = 8;
   static constexpr int kU = 4;
   static constexpr int kEntry = static_cast<int>(sizeof(T));
-  static constexpr int kTableBytes = table::bytes(256);
+  static constexpr int kTableBytes = table::bytes(512);
   static constexpr bool kExactLanes = false;
 
-  __device__ static void prepare(const dot_params &p, unsigned char *smem) {
-    table::fill(reinterpret_cast<T *>(smem), static_cast<const T *>(p.table), 256);
+  // signed entry i of the product table `g` (256 magnitudes)
+  __device__ __forceinline__ static T signed_entry(const T *g, int i) {
+    const int h = i & 255;
+    if (h == 0) return T(0);
+    return i >= 256 ? -g[h] : g[h];
   }
 
-  template <int K> __device__ __forceinline__ static uint32_t spread(uint32_t v) {
+  __device__ static void prepare(const dot_params &p, unsigned char *smem) {
+    const T *g = static_cast<const T *>(p.table);
+    T *s = reinterpret_cast<T *>(smem);
+    for (int e = threadIdx.x; e < 512 * table::kCopies; e += blockDim.x)
+      s[e] = signed_entry(g, e / table::kCopies);
+  }
+
+  template <int K> __device__ __forceinline__ static uint32_t permute(uint32_t a, uint32_t b) {
     uint32_t r;
-    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(v), "r"(0u), "n"(0x8888 + 0x1111 * K));
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "n"(K));
     return r;
   }
 
-  // entry `index` of this lane's copy, zeroed unless `mask`, sign bit `sign`
-  __device__ __forceinline__ static T product(const unsigned char *smem, uint32_t index,
-                                              uint32_t lane_off, uint32_t mask, uint32_t sign) {
-    const unsigned char *at = smem + (index * table::kEntryBytes + lane_off);
-    if constexpr (sizeof(T) == 4) {
-      const uint32_t t = *reinterpret_cast<const uint32_t *>(at);
-      return __uint_as_float((t & mask) | sign);
-    } else {
-      const uint2 t = *reinterpret_cast<const uint2 *>(at);
-      return __hiloint2double(static_cast<int>((t.y & mask) | sign), static_cast<int>(t.x & mask));
-    }
+  // table index of pair k: byte k of `sums` | byte k of `signs` << 8 (the
+  // upper bytes replicate bit 7 of a sign byte, which is 0)
+  template <int K> __device__ __forceinline__ static uint32_t index(uint32_t sums, uint32_t signs) {
+    constexpr int c = 8 | (4 + K);
+    return permute<(c << 12) | (c << 8) | ((4 + K) << 4) | K>(sums, signs);
   }
 
   template <class Acc>
-  __device__ __forceinline__ static void add(Acc &acc, int slot, T p) {
+  __device__ __forceinline__ static void add(Acc &acc, int slot, const unsigned char *smem,
+                                             uint32_t index, uint32_t lane_off) {
+    const T p = table::at(smem, index, lane_off);
     if constexpr (sizeof(T) == 4)
       acc.mac(slot, p, 1.0f);
     else
@@ -439,26 +448,22 @@ template <typename T> struct lns8_fused_codec {
       const uint32_t x = xw[w], y = yw[w];
       const uint32_t bx = (x & 0x7f7f7f7fu) ^ 0x40404040u;
       const uint32_t by = (y & 0x7f7f7f7fu) ^ 0x40404040u;
-      const uint32_t h = bx + by;  // byte k: biased product log of pair k
       // bit 7 of each byte: that code is not reserved
       const uint32_t lx = bx + 0x7f7f7f7fu, ly = by + 0x7f7f7f7fu;
       nan |= (x & ~lx) | (y & ~ly);  // reserved with the sign bit set
-      const uint32_t live = lx & ly;
-      const uint32_t sg = x ^ y;  // product signs at bits 7, 15, 23, 31
-      add(acc, 4 * w + 0, product(smem, __byte_perm(h, 0u, 0x4440u), lane_off,
-                                  spread<0>(live), (sg << 24) & 0x80000000u));
-      add(acc, 4 * w + 1, product(smem, __byte_perm(h, 0u, 0x4441u), lane_off,
-                                  spread<1>(live), (sg << 16) & 0x80000000u));
-      add(acc, 4 * w + 2, product(smem, __byte_perm(h, 0u, 0x4442u), lane_off,
-                                  spread<2>(live), (sg << 8) & 0x80000000u));
-      add(acc, 4 * w + 3, product(smem, h >> 24, lane_off, spread<3>(live),
-                                  sg & 0x80000000u));
+      // byte k: biased product log of pair k, 0 when an operand is zero
+      const uint32_t h = (bx + by) & permute<0xba98>(lx & ly, 0u);
+      const uint32_t sg = ((x ^ y) & 0x80808080u) >> 7;  // byte k: sign of pair k
+      add(acc, 4 * w + 0, smem, index<0>(h, sg), lane_off);
+      add(acc, 4 * w + 1, smem, index<1>(h, sg), lane_off);
+      add(acc, 4 * w + 2, smem, index<2>(h, sg), lane_off);
+      add(acc, 4 * w + 3, smem, index<3>(h, sg), lane_off);
     }
     if (nan & 0x80808080u) {
       if constexpr (sizeof(T) == 4)
-        add(acc, 0, __uint_as_float(0x7fc00000u));
+        acc.mac(0, __uint_as_float(0x7fc00000u), 1.0f);
       else
-        add(acc, 0, __hiloint2double(0x7ff80000, 0));
+        acc.mac_d(0, __hiloint2double(0x7ff80000, 0), 1.0);
     }
   }
 
@@ -473,9 +478,9 @@ template <typename T> struct lns8_fused_codec {
     if ((bx == 0 && (cx & 0x80u)) || (by == 0 && (cy & 0x80u))) {
       v = __hiloint2double(0x7ff80000, 0);
     } else {
-      const uint32_t mask = (bx == 0 || by == 0) ? 0u : 0xffffffffu;
-      const uint32_t lane_off = table::lane_offset();
-      v = static_cast<double>(product(smem, bx + by, lane_off, mask, ((cx ^ cy) & 0x80u) << 24));
+      const uint32_t h = (bx == 0 || by == 0) ? 0u : bx + by;
+      v = static_cast<double>(
+          table::at(smem, h | (((cx ^ cy) & 0x80u) << 1), table::lane_offset()));
     }
     acc.mac_d(0, v, 1.0);
   }
