@@ -321,10 +321,11 @@ template <typename T, int C = 32> struct lane_table {
 };
 
 // lns8_r3 (one code per byte): a full 256-entry decode table in per-lane
-// copies (lane_table).  Table values come from the host exp2f / exp2 and are
-// the reference's decoded values bit for bit.
-template <typename T> struct lns8_codec {
-  using table = lane_table<T>;
+// copies (lane_table; C copies, 32 for the DOTs, 16 for the FP64 GEMV rows).
+// Table values come from the host exp2f / exp2 and are the reference's
+// decoded values bit for bit.
+template <typename T, int C = 32> struct lns8_codec {
+  using table = lane_table<T, C>;
   static constexpr int kS = 8;
   static constexpr int kW = 8;
   static constexpr int kU = 4;
@@ -1764,9 +1765,14 @@ __device__ __forceinline__ float fma_bf16(uint32_t a_top, uint32_t pair, float c
 // stage 8 KiB of rows and take the third stage (see gemv_rows).
 constexpr int gemv_ring(int s) { return (s == 16 || s == 9 ? 128 : 96) * 1024; }
 
+// FP64 rows of lns8_r3 (the vector held as FP64 values): 32 codes per
+// thread and a 32 KiB stage ring beside the 32 KiB table, two blocks per SM.
+template <class Codec> constexpr bool is_lns8_f64 = std::is_same_v<Codec, lns8_codec<double, 16>>;
+
 template <class Codec>
-using gemv_shape = tma_shape<Codec::kS, gemv_ring(Codec::kS),
-                             (tma_vpt(Codec::kS) > 32 ? tma_vpt(Codec::kS) : 32)>;
+using gemv_shape = tma_shape<Codec::kS, is_lns8_f64<Codec> ? 64 * 1024 : gemv_ring(Codec::kS),
+                             is_lns8_f64<Codec> ? 32
+                                                : (tma_vpt(Codec::kS) > 32 ? tma_vpt(Codec::kS) : 32)>;
 
 __device__ __forceinline__ void gemv_publish(const gemv_params &g, uint32_t r, double v) {
   g.partials[static_cast<uint64_t>(r) * gridDim.x + blockIdx.x] = v;
@@ -1854,11 +1860,13 @@ __global__ void __launch_bounds__(kThreads, Codec::kS == 12 || F64 ? 3 : 1)
   // this thread's codes of the vector segment, decoded once: codes of up to
   // 16 bits are bf16 values exactly and are kept as bf16 pairs (half the
   // registers, so more blocks fit an SM); wider ones as FP32; e2m3 codes as
-  // the f16 pairs of the hardware conversion; lns8_r3 codes as the FP32
-  // values of their per-lane table
+  // the f16 pairs of the hardware conversion; lns8_r3 codes as the FP32 (or,
+  // for FP64 rows, FP64) values of their per-lane table
   constexpr bool kLns = std::is_same_v<Codec, lns8_codec<float>>;
-  constexpr bool kPairs = W <= 16 && !kLns;
-  float vec[kPairs ? 1 : VPT];
+  constexpr bool kLns64 = is_lns8_f64<Codec>;
+  constexpr bool kPairs = W <= 16 && !kLns && !kLns64;
+  float vec[kPairs || kLns64 ? 1 : VPT];
+  double vecd[kLns64 ? VPT : 1];
   uint32_t vec2[kPairs ? VPT / 2 : 1];
   {
     const uint32_t *vw = reinterpret_cast<const uint32_t *>(
@@ -1877,12 +1885,17 @@ __global__ void __launch_bounds__(kThreads, Codec::kS == 12 || F64 ? 3 : 1)
         }
         continue;
       }
-      if constexpr (kLns) {
+      if constexpr (kLns || kLns64) {
         const uint32_t lane_off = Codec::table::lane_offset();
 #pragma unroll
-        for (int i = 0; i < UV * GROUP; ++i)
-          vec[v * UV * GROUP + i] =
+        for (int i = 0; i < UV * GROUP; ++i) {
+          const auto dv =
               Codec::table::at(smem, __byte_perm(w[i >> 2], 0u, 0x4440u + (i & 3)), lane_off);
+          if constexpr (kLns64)
+            vecd[v * UV * GROUP + i] = dv;
+          else
+            vec[v * UV * GROUP + i] = dv;
+        }
         continue;
       }
 #pragma unroll
@@ -1919,7 +1932,7 @@ __global__ void __launch_bounds__(kThreads, Codec::kS == 12 || F64 ? 3 : 1)
       ok = mbar_wait(&full[st], ph) && ok;
       const uint32_t *ws = reinterpret_cast<const uint32_t *>(ring + st * TILE_BYTES);
       float c0 = 0.f, c1 = 0.f;
-      double d0 = 0.0;  // F64
+      double d0 = 0.0, d1 = 0.0;  // F64, kLns64
 #pragma unroll
       for (int v = 0; v < V / GROUP; ++v) {
         const int u = threadIdx.x + v * kThreads;
@@ -1951,6 +1964,22 @@ __global__ void __launch_bounds__(kThreads, Codec::kS == 12 || F64 ? 3 : 1)
               c1 = fmaf(mv, vec[j], c1);
             else
               c0 = fmaf(mv, vec[j], c0);
+          }
+          continue;
+        }
+        if constexpr (kLns64) {
+          // exact products of the decoded FP64 values, values 2k and 2k + 1
+          // on one chain (as the DOT's FP64 accumulator)
+          const uint32_t lane_off = Codec::table::lane_offset();
+#pragma unroll
+          for (int i = 0; i < UV * GROUP; ++i) {
+            const int j = v * UV * GROUP + i;
+            const double mv =
+                Codec::table::at(smem, __byte_perm(w[i >> 2], 0u, 0x4440u + (i & 3)), lane_off);
+            if ((i >> 1) & 1)
+              d1 = fma(mv, vecd[j], d1);
+            else
+              d0 = fma(mv, vecd[j], d0);
           }
           continue;
         }
@@ -2029,6 +2058,8 @@ __global__ void __launch_bounds__(kThreads, Codec::kS == 12 || F64 ? 3 : 1)
       }
       if constexpr (F64) {
         red[(k + h) * kThreads + threadIdx.x] = d0;
+      } else if constexpr (kLns64) {
+        red[(k + h) * kThreads + threadIdx.x] = d0 + d1;
       } else {
         red[(k + h) * kThreads + threadIdx.x] =
             static_cast<double>(c0) + static_cast<double>(c1);
@@ -2668,8 +2699,8 @@ gemv_entry make_gemv_entry() {
 }
 
 // The vector-once kernels: FP32 rows of the E8 codes, raw FP32 and
-// lns8_r3 (its per-lane table); FP64 rows of the E8 codes and raw FP32;
-// e2m3 rows (exact) for both.
+// lns8_r3 (its per-lane table); FP64 rows of the E8 codes, raw FP32 and
+// lns8_r3 (the FP64 table); e2m3 rows (exact) for both.
 static gemv_entry gemv_lookup(int32_t format, int32_t layout, int32_t accum) {
   using namespace aut::dev;
   const bool dense = layout == AUT_LAYOUT_DENSE;
@@ -2687,6 +2718,7 @@ static gemv_entry gemv_lookup(int32_t format, int32_t layout, int32_t accum) {
     case AUT_FMT_E8M15:
       return dense ? make_gemv_entry<e8_codec<24, 24>, true>() : make_gemv_entry<e8_codec<32, 24>, true>();
     case AUT_FMT_FP32: return make_gemv_entry<e8_codec<32, 32>, true>();
+    case AUT_FMT_LNS8_R3: return make_gemv_entry<lns8_codec<double, 16>>();
     case AUT_FMT_E2M3: break;
     default: return {};
     }
@@ -2759,7 +2791,8 @@ aut_status gemv_launch(aut_workspace *ws, int32_t format, int32_t layout, int32_
     const code_tables *t = nullptr;
     st = code_tables_for(ws, format, &t);
     if (st != AUT_OK) return st;
-    table = t->full_f32;
+    table = accum == AUT_ACCUM_FP64 ? static_cast<const void *>(t->full_f64)
+                                    : static_cast<const void *>(t->full_f32);
   }
   const uint64_t row_bytes = segments * e.tile_bytes;
   const uint64_t cap = static_cast<uint64_t>(ws->sm_count) * per_sm;

@@ -128,8 +128,10 @@ def test_gemv_degenerate_shapes(ws):
 VECTOR_ONCE = ["e8m0", "e8m1", "e8m3", "e8m5", "bf16_e8m7", "e8m15", "fp32", "e2m3", "lns8_r3"]
 
 
-# FP64 rows decode the vector once for the E8 codes and raw FP32
-VECTOR_ONCE_F64 = ["e8m0", "e8m1", "e8m3", "e8m5", "bf16_e8m7", "e8m15", "fp32", "e2m3"]
+# FP64 rows decode the vector once for the E8 codes, raw FP32, e2m3 and
+# lns8_r3 (its FP64 table; 8192 values per tile)
+VECTOR_ONCE_F64 = ["e8m0", "e8m1", "e8m3", "e8m5", "bf16_e8m7", "e8m15", "fp32", "e2m3",
+                   "lns8_r3"]
 
 
 @pytest.mark.parametrize("name", VECTOR_ONCE)
