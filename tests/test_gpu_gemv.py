@@ -268,3 +268,35 @@ def test_gemv_e2m3_rows_are_exact(ws, orc, layout, accum):
     for r in range(rows):
         d, _ = ref(r)
         assert got[r] == float(np.longdouble(d[0]) + np.longdouble(d[1])), (layout, accum, r)
+
+
+@pytest.mark.parametrize("accum", [0, 1])
+def test_gemv_lns8_reserved_codes(ws, orc, accum):
+    """lns8_r3 rows on the vector-once kernel (the FP32 and the FP64 table):
+    the reserved code decodes to zero with its sign bit clear and to NaN with
+    it set, in the matrix and in the vector; a NaN reaches only its row."""
+    import torch
+    from accessor_universal_test_b200 import _lib
+    rows, columns = 24, 16384
+    fid = _lib.format_id("lns8_r3")
+    desc = _lib.format_info(fid)
+    mc = orc.encode(desc, orc.synthetic(3, SEED, 0, rows * columns))
+    vc = orc.encode(desc, orc.synthetic(3, SEED, 1, columns))
+    mc[2 * columns + 17] = 0x40    # zero
+    mc[2 * columns + 18] = 0x40
+    mc[5 * columns + 4000] = 0xc0  # NaN
+    mc[9 * columns:10 * columns] = 0x40  # a row of zeros
+    vc[123] = 0x40                 # a zero in the vector touches every row
+    bufs = [torch.from_numpy(orc.pack_dense(8, c).view(np.uint8).copy()).cuda() for c in (mc, vc)]
+    got = _gemv(ws, "lns8_r3", 0, accum, bufs[0], bufs[1], rows, columns)
+    for r in range(rows):
+        if r == 5:
+            assert np.isnan(got[r]), got[r]
+            continue
+        d, s = orc.dot_codes(desc, mc[r * columns:(r + 1) * columns], vc, threads=1)
+        want = np.longdouble(d[0]) + np.longdouble(d[1])
+        sabs = np.longdouble(s[0]) + np.longdouble(s[1])
+        if r == 9:
+            assert got[r] == 0.0, got[r]
+            continue
+        assert normalized_error(got[r], want, sabs) <= TOL[accum], (r, got[r], float(want))
