@@ -6,9 +6,9 @@ LNS kernel (lns_benchmark_kernels.cuh:80-131), compiled from its headers for
 sm_100a (oracle/_ref/librefgpu.so) and launched the way its benchmarks
 launch them, run on the very device buffers libautdot reads, at the
 benchmark's sizes.  Both DOTs are compared with the reference's compensated
-long-double CPU DOT of the same codes.  The north star asks that the
-normalised error be no worse than the reference's own kernel for the same
-format and accumulator.  Asserted for every exact decoder of the
+long-double CPU DOT of the same codes.  The library's normalised error
+must be no worse than the reference's own kernel for the same format and
+accumulator.  Asserted for every exact decoder of the
 reference: within the stated bound, and no worse than the reference
 kernel's error, except where both sit far below any meaningful level --
 FP64 errors up to 1e-19 (the summation order decides them), and LNS with
