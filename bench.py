@@ -486,7 +486,7 @@ def run_per_config(ws, stream, threads, peak, reuse_refs):
     if ws.status() != 0:
         raise RuntimeError("a bounded device wait timed out during the configurations")
 
-    # config 2's size sweep: launch-bound to HBM-bound (small sizes stay in L2)
+    # the raw FP32/FP64 size sweep, 2^10 to 2^27: launch-bound to HBM-bound (small sizes stay in L2)
     sweep = []
     for name, kind, acc in (("fp32", 1, _lib.ACC_FP32), ("fp64", 0, _lib.ACC_FP64)):
         fid = _lib.format_id(name)
